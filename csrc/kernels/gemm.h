@@ -1,0 +1,46 @@
+// Host-side interface of the tcgen05 GEMM (gemm_tcgen05.cu) and of the
+// fp32 SIMT GEMM (gemm_f32.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace uhfs {
+
+enum GemmEpilogue : int {
+  GEMM_EPI_BF16 = 0,       // C = acc (+ bias)                       bf16 out
+  GEMM_EPI_BIAS_GELU = 1,  // aux_out = acc + bias; C = gelu(aux_out) bf16 out
+  GEMM_EPI_RESID = 2,      // C = acc (+ bias) + aux                  bf16 out (C may alias aux)
+  GEMM_EPI_DGELU = 3,      // C = acc * gelu'(aux)                    bf16 out
+  GEMM_EPI_F32_ACCUM = 4,  // C += acc   (fp32, atomic: split-K safe)
+  GEMM_EPI_F32_STORE = 5,  // C = acc    (fp32)
+};
+
+struct GemmProblem {
+  int M = 0, N = 0, K = 0;
+  const __nv_bfloat16* A = nullptr;  // K-major: A[m*lda + k]; MN-major: A[k*lda + m]
+  long long lda = 0;
+  bool a_mn = false;
+  const __nv_bfloat16* B = nullptr;  // K-major: B[n*ldb + k]; MN-major: B[k*ldb + n]
+  long long ldb = 0;
+  bool b_mn = false;
+  void* C = nullptr;
+  long long ldc = 0;
+  int epi = GEMM_EPI_BF16;
+  const __nv_bfloat16* bias = nullptr;
+  const __nv_bfloat16* aux = nullptr;
+  long long ld_aux = 0;
+  __nv_bfloat16* aux_out = nullptr;
+  long long ld_aux_out = 0;
+  int splits = 1;     // split-K factor (only meaningful with GEMM_EPI_F32_ACCUM)
+  int block_n = 0;    // 0 = choose, else 128 or 256
+  int max_ctas = 0;   // 0 = one per SM
+};
+
+void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream);
+
+// C[M,N] (fp32) = A[M,K] (fp32, row-major) x B (fp32): b_trans=false -> B[K,N], true -> B[N,K].
+// Exact fp32 FMA accumulation (the fp32 contract of the public matmul).
+void gemm_f32_simt(const float* A, const float* B, float* C, int M, int N, int K, bool b_trans, cudaStream_t stream);
+
+}  // namespace uhfs

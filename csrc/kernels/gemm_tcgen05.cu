@@ -1,0 +1,483 @@
+// Persistent, warp-specialized bf16 GEMM on the sm_100a 5th-generation tensor
+// core (tcgen05.mma kind::f16, fp32 accumulators in TMEM), fed by TMA.
+//
+//   C[M,N] = sum_k A(m,k) * B(n,k)      (+ fused epilogue)
+//
+// A and B are each either K-major (row-major with K contiguous) or MN-major
+// (K rows, M/N contiguous).  This covers every Linear layout without a
+// transpose copy:
+//   forward  Y  = X  W^T   A=X  (K-major), B=W  (K-major)
+//   dgrad    dX = dY W     A=dY (K-major), B=W  (MN-major)
+//   wgrad    dW = dY^T X   A=dY (MN-major), B=X (MN-major)
+//
+// Replaces the reference's cublasSgemm call in CudaTensorF32::matmul
+// (cuda/kernels.cu:488-493) and its Python matmul (tensor.py:609-675).
+//
+// CTA layout (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (one elected lane), 128B-swizzled tiles, no
+//               multicast (this kernel also runs inside multi-GPU jobs)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes each, fused bias / GELU /
+//               residual / dGELU / fp32-accumulate, vectorized stores
+// The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of
+// tile i overlaps the main loop of tile i+1.  Every wait is bounded.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "gemm.h"
+
+namespace uhfs {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;           // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kSmemBudget = 200 * 1024;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (kSmemBudget - 2048) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_per_split, kb_total;
+  void* C;
+  long long ldc;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* aux;
+  long long ld_aux;
+  __nv_bfloat16* aux_out;
+  long long ld_aux_out;
+  DeviceStatus* status;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, int& tn, int& split) {
+  const int mn_tiles = a.tiles_m * a.tiles_n;
+  split = t / mn_tiles;
+  int mn = t - split * mn_tiles;
+  // Grouped raster: walk 16 M-tiles down a column of N before moving right,
+  // so concurrently running CTAs share B tiles in L2.
+  constexpr int G = 16;
+  const int group_span = G * a.tiles_n;
+  const int g = mn / group_span;
+  const int first_m = g * G;
+  const int gm = min(a.tiles_m - first_m, G);
+  const int r = mn - g * group_span;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v, int valid_cols) {
+  if (valid_cols >= 32) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+      *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<uint4*>(h);
+    }
+  } else {
+    for (int q = 0; q < 4; ++q) {
+      if (q * 8 >= valid_cols) break;
+      __align__(16) __nv_bfloat162 h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+      *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<uint4*>(h);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v, int valid_cols) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (q * 8 < valid_cols) {
+      uint4 raw = *reinterpret_cast<const uint4*>(src + q * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        v[q * 8 + 2 * j] = f.x;
+        v[q * 8 + 2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[q * 8 + j] = 0.f;
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr uint32_t kIdesc = make_idesc(1 /*bf16*/, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* done = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_units = args.tiles_m * args.tiles_n * args.splits;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x) {
+        int tm, tn, split;
+        tile_coords(args, t, tm, tn, split);
+        const int m0 = tm * BM, n0 = tn * BN;
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.status, kErrWaitTimeoutEmpty, 10)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = tiles + stage * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c) tma_load_2d(sA + c * (64 * BK * 2), &tmA, &full[stage], m0 + 64 * c, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sB + c * (64 * BK * 2), &tmB, &full[stage], n0 + 64 * c, k0);
+          }
+          issued_mask |= (1u << stage);
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave the CTA with bulk copies still landing in shared memory.
+      for (int s = 0; s < S; ++s)
+        if (issued_mask & (1u << s)) mbar_wait_bounded(&full[s], (issued_parity >> s) & 1u, args.status, kErrWaitTimeoutFull, 11);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x) {
+        int tm, tn, split;
+        tile_coords(args, t, tm, tn, split);
+        const int kb0 = split * args.kb_per_split;
+        const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 20)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, args.status, kErrWaitTimeoutFull, 21)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(tiles + stage * Cfg::kStageBytes);
+          const uint32_t b_base = a_base + Cfg::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t adesc, bdesc;
+            if constexpr (!A_MN)
+              adesc = make_smem_desc(a_base + kk * 32, 16, 1024, kSwizzle128B);
+            else
+              adesc = make_smem_desc(a_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
+            if constexpr (!B_MN)
+              bdesc = make_smem_desc(b_base + kk * 32, 16, 1024, kSwizzle128B);
+            else
+              bdesc = make_smem_desc(b_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
+            tc_mma_f16(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);  // frees this smem stage once the MMAs retire
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // All MMAs issued by this thread retire before TMEM is released.
+      tc_commit(done);
+      mbar_wait_bounded(done, 0, args.status, kErrWaitTimeoutAccum, 22);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_units; t += gridDim.x) {
+      int tm, tn, split;
+      tile_coords(args, t, tm, tn, split);
+      const int m0 = tm * BM, n0 = tn * BN;
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const bool row_ok = row < args.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= args.N) break;  // warp-uniform
+        float v[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32);
+        tmem_ld_32x32b_x32(taddr, v);
+        tc_wait_ld();
+        const int valid = min(32, args.N - col0);
+        if constexpr (EPI == GEMM_EPI_BF16 || EPI == GEMM_EPI_BIAS_GELU || EPI == GEMM_EPI_RESID) {
+          if (args.bias != nullptr) {
+            float b[32];
+            load_bf16x32(args.bias + col0, b, valid);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += b[j];
+          }
+        }
+        if (!row_ok) continue;
+        if constexpr (EPI == GEMM_EPI_BF16) {
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+        } else if constexpr (EPI == GEMM_EPI_BIAS_GELU) {
+          store_bf16x32(args.aux_out + (long long)row * args.ld_aux_out + col0, v, valid);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+        } else if constexpr (EPI == GEMM_EPI_RESID) {
+          float r[32];
+          load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += r[j];
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+        } else if constexpr (EPI == GEMM_EPI_DGELU) {
+          float u[32];
+          load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad(u[j]);
+          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+        } else if constexpr (EPI == GEMM_EPI_F32_ACCUM) {
+          float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q * 4 < valid)
+              atomicAdd(reinterpret_cast<float4*>(dst + q * 4), make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+        } else {  // GEMM_EPI_F32_STORE
+          float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q * 4 < valid)
+              *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------- host
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128-byte swizzle, box {64, box_outer}.
+CUtensorMap make_tmap(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                      uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("gemm operand must be 16-byte aligned");
+  if ((row_stride_elems * 2) % 16 != 0) throw std::runtime_error("gemm leading dimension must be a multiple of 8");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch(const GemmProblem& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set = true;
+  }
+  // A: K-major [M][lda] -> dims {K, M}; MN-major [K][lda] -> dims {M, K}
+  CUtensorMap ta = A_MN ? make_tmap(p.A, p.M, p.K, p.lda, BK) : make_tmap(p.A, p.K, p.M, p.lda, BM);
+  CUtensorMap tb = B_MN ? make_tmap(p.B, p.N, p.K, p.ldb, BK) : make_tmap(p.B, p.K, p.N, p.ldb, BN);
+  GemmArgs a;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.tiles_m = (p.M + BM - 1) / BM;
+  a.tiles_n = (p.N + BN - 1) / BN;
+  a.kb_total = (p.K + BK - 1) / BK;
+  int splits = p.splits < 1 ? 1 : p.splits;
+  if (splits > a.kb_total) splits = a.kb_total;
+  a.kb_per_split = (a.kb_total + splits - 1) / splits;
+  a.splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;  // no empty splits
+  a.C = p.C;
+  a.ldc = p.ldc;
+  a.bias = p.bias;
+  a.aux = p.aux;
+  a.ld_aux = p.ld_aux;
+  a.aux_out = p.aux_out;
+  a.ld_aux_out = p.ld_aux_out;
+  a.status = device_status_ptr();
+  const int units = a.tiles_m * a.tiles_n * a.splits;
+  int grid = units < num_sms() ? units : num_sms();
+  if (p.max_ctas > 0 && grid > p.max_ctas) grid = p.max_ctas;
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int BN>
+void dispatch_bn(const GemmProblem& p, cudaStream_t s) {
+  const bool am = p.a_mn, bm = p.b_mn;
+  switch (p.epi) {
+    case GEMM_EPI_BF16:
+      if (!am && !bm) return launch<BN, false, false, GEMM_EPI_BF16>(p, s);
+      if (!am && bm) return launch<BN, false, true, GEMM_EPI_BF16>(p, s);
+      if (am && !bm) return launch<BN, true, false, GEMM_EPI_BF16>(p, s);
+      return launch<BN, true, true, GEMM_EPI_BF16>(p, s);
+    case GEMM_EPI_BIAS_GELU:
+      if (!am && !bm) return launch<BN, false, false, GEMM_EPI_BIAS_GELU>(p, s);
+      break;
+    case GEMM_EPI_RESID:
+      if (!am && !bm) return launch<BN, false, false, GEMM_EPI_RESID>(p, s);
+      if (!am && bm) return launch<BN, false, true, GEMM_EPI_RESID>(p, s);
+      break;
+    case GEMM_EPI_DGELU:
+      if (!am && bm) return launch<BN, false, true, GEMM_EPI_DGELU>(p, s);
+      break;
+    case GEMM_EPI_F32_ACCUM:
+      if (am && bm) return launch<BN, true, true, GEMM_EPI_F32_ACCUM>(p, s);
+      if (!am && bm) return launch<BN, false, true, GEMM_EPI_F32_ACCUM>(p, s);
+      break;
+    case GEMM_EPI_F32_STORE:
+      if (!am && !bm) return launch<BN, false, false, GEMM_EPI_F32_STORE>(p, s);
+      if (!am && bm) return launch<BN, false, true, GEMM_EPI_F32_STORE>(p, s);
+      if (am && bm) return launch<BN, true, true, GEMM_EPI_F32_STORE>(p, s);
+      break;
+    default:
+      break;
+  }
+  throw std::runtime_error("gemm: unsupported (layout, epilogue) combination");
+}
+
+}  // namespace
+
+void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0) return;
+  if (p.K <= 0) throw std::runtime_error("gemm: K must be positive");
+  if (p.N % 8 != 0) throw std::runtime_error("gemm: N must be a multiple of 8");
+  if (p.ldc % 8 != 0 && p.epi != GEMM_EPI_F32_ACCUM && p.epi != GEMM_EPI_F32_STORE)
+    throw std::runtime_error("gemm: ldc must be a multiple of 8");
+  if ((p.epi == GEMM_EPI_F32_ACCUM || p.epi == GEMM_EPI_F32_STORE) && p.ldc % 4 != 0)
+    throw std::runtime_error("gemm: fp32 ldc must be a multiple of 4");
+  int bn = p.block_n;
+  if (bn != 128 && bn != 256) bn = (p.N <= 128) ? 128 : 256;
+  if (bn == 256) dispatch_bn<256>(p, stream);
+  else dispatch_bn<128>(p, stream);
+}
+
+}  // namespace uhfs

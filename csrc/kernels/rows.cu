@@ -1,0 +1,404 @@
+// Row-wise kernels: RMSNorm fwd/bwd, token+position embedding gather /
+// scatter-add, fused softmax cross-entropy, row softmax.
+//
+// The reference computes all of these in pure Python over list storage
+// (RMSNorm nn.py:166-181, Embedding nn.py:184-217, cross_entropy
+// functional.py:20-76, softmax tensor.py:966-1027).  Here one warp (RMSNorm,
+// embedding) or one CTA (cross-entropy over a 32K vocabulary) owns a row; all
+// loads are 16-byte vectors, statistics are fp32, and the cross-entropy kernel
+// emits the logits gradient in the same pass that computes the loss.
+#include <stdexcept>
+
+#include "kernels.h"
+#include "vec.cuh"
+
+namespace uhfs {
+
+namespace {
+
+bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ RMSNorm
+template <typename T>
+__global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                                   float* __restrict__ rstd, int rows, int cols, float eps, bool vec) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const T* xr = x + (long long)row * cols;
+    float ss = 0.f;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float f[8];
+      load8_guard<T>(xr + c, f, c, cols, vec);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)cols + eps);
+    if (lane == 0 && rstd != nullptr) rstd[row] = r;
+    T* yr = y + (long long)row * cols;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float f[8], g[8];
+      load8_guard<T>(xr + c, f, c, cols, vec);
+      load8_guard<T>(w + c, g, c, cols, vec);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = f[i] * r * g[i];
+      store8_guard<T>(yr + c, f, c, cols, vec);
+    }
+  }
+}
+
+// dx_i = r * (g_i - x_i * r^2 * sum_j(g_j x_j) / n),   g = dy * w
+template <typename T>
+__global__ void rmsnorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
+                                      const float* __restrict__ rstd, const T* __restrict__ dres, T* __restrict__ dx,
+                                      int rows, int cols, bool vec) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const long long off = (long long)row * cols;
+    float dot = 0.f;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float a[8], b[8], g[8];
+      load8_guard<T>(dy + off + c, a, c, cols, vec);
+      load8_guard<T>(x + off + c, b, c, cols, vec);
+      load8_guard<T>(w + c, g, c, cols, vec);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot += a[i] * g[i] * b[i];
+    }
+    dot = warp_sum(dot);
+    const float r = rstd[row];
+    const float coef = r * r * dot / (float)cols;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float a[8], b[8], g[8], o[8];
+      load8_guard<T>(dy + off + c, a, c, cols, vec);
+      load8_guard<T>(x + off + c, b, c, cols, vec);
+      load8_guard<T>(w + c, g, c, cols, vec);
+      if (dres != nullptr) {
+        load8_guard<T>(dres + off + c, o, c, cols, vec);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += r * (a[i] * g[i] - b[i] * coef);
+      store8_guard<T>(dx + off + c, o, c, cols, vec);
+    }
+  }
+}
+
+// dw_j += sum_rows dy_rj * x_rj * r_r; one thread per column pair-of-4, 128 rows per block-row.
+template <typename T>
+__global__ void rmsnorm_bwd_dw_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                      const float* __restrict__ rstd, float* __restrict__ dw, int rows, int cols) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int r0 = blockIdx.y * 128;
+  const int r1 = min(rows, r0 + 128);
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const long long o = (long long)r * cols + c;
+    acc += to_float<T>(dy[o]) * to_float<T>(x[o]) * rstd[r];
+  }
+  atomicAdd(dw + c, acc);
+}
+
+// ---------------------------------------------------------------- embedding
+template <typename T>
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ tok,
+                                     const T* __restrict__ pos, T* __restrict__ out, int rows, int dim, int seq_len,
+                                     bool vec) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const long long id = ids[row];
+    const T* tr = tok + id * dim;
+    const T* pr = pos != nullptr ? pos + (long long)(row % seq_len) * dim : nullptr;
+    T* orow = out + (long long)row * dim;
+    for (int c = lane * 8; c < dim; c += 256) {
+      float a[8];
+      load8_guard<T>(tr + c, a, c, dim, vec);
+      if (pr != nullptr) {
+        float b[8];
+        load8_guard<T>(pr + c, b, c, dim, vec);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] += b[i];
+      }
+      store8_guard<T>(orow + c, a, c, dim, vec);
+    }
+  }
+}
+
+template <typename T>
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ dout,
+                                     float* __restrict__ dtok, float* __restrict__ dpos, int rows, int dim,
+                                     int seq_len, bool vec) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+    const long long id = ids[row];
+    const T* dr = dout + (long long)row * dim;
+    float* tr = dtok != nullptr ? dtok + id * dim : nullptr;
+    float* pr = dpos != nullptr ? dpos + (long long)(row % seq_len) * dim : nullptr;
+    for (int c = lane * 8; c < dim; c += 256) {
+      float a[8];
+      load8_guard<T>(dr + c, a, c, dim, vec);
+      if (vec && c + 8 <= dim) {
+        if (tr) {
+          atomicAdd(reinterpret_cast<float4*>(tr + c), make_float4(a[0], a[1], a[2], a[3]));
+          atomicAdd(reinterpret_cast<float4*>(tr + c + 4), make_float4(a[4], a[5], a[6], a[7]));
+        }
+        if (pr) {
+          atomicAdd(reinterpret_cast<float4*>(pr + c), make_float4(a[0], a[1], a[2], a[3]));
+          atomicAdd(reinterpret_cast<float4*>(pr + c + 4), make_float4(a[4], a[5], a[6], a[7]));
+        }
+      } else {
+        for (int i = 0; i < 8 && c + i < dim; ++i) {
+          if (tr) atomicAdd(tr + c + i, a[i]);
+          if (pr) atomicAdd(pr + c + i, a[i]);
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------- softmax + CE
+constexpr int kCeThreads = 512;
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+  m = mn;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads) softmax_ce_kernel(const T* __restrict__ logits, long long ld,
+                                                                const int64_t* __restrict__ targets,
+                                                                float* __restrict__ loss_rows, T* dlogits, int cols,
+                                                                float grad_scale, const float* grad_scale_ptr,
+                                                                bool vec) {
+  const int row = blockIdx.x;
+  const T* lr = logits + (long long)row * ld;
+  __shared__ float sm_m[kCeThreads / 32], sm_s[kCeThreads / 32];
+  __shared__ float row_max, row_sum;
+  float m = -INFINITY, s = 0.f;
+  for (int c = threadIdx.x * 8; c < cols; c += kCeThreads * 8) {
+    float f[8];
+    load8_guard<T>(lr + c, f, c, cols, vec);
+    float lm = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (c + i < cols) lm = fmaxf(lm, f[i]);
+    float ls = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (c + i < cols) ls += __expf(f[i] - lm);
+    online_merge(m, s, lm, ls);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm_m[threadIdx.x >> 5] = m;
+    sm_s[threadIdx.x >> 5] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < kCeThreads / 32 ? sm_m[threadIdx.x] : -INFINITY;
+    s = threadIdx.x < kCeThreads / 32 ? sm_s[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      online_merge(m, s, m2, s2);
+    }
+    if (threadIdx.x == 0) {
+      row_max = m;
+      row_sum = s;
+    }
+  }
+  __syncthreads();
+  const float mx = row_max;
+  const float inv = 1.0f / row_sum;
+  const long long tgt = targets[row];
+  if (threadIdx.x == 0) {
+    const float xt = to_float<T>(lr[tgt]);
+    // -log(max(p_t, 1e-30)) as in the reference, computed in log space.
+    const float nll = logf(row_sum) + mx - xt;
+    loss_rows[row] = fminf(nll, 69.07755279f);
+  }
+  if (dlogits == nullptr) return;
+  if (grad_scale_ptr != nullptr) grad_scale *= *grad_scale_ptr;
+  // Every thread has read its slice of the row above; the block barrier makes
+  // the in-place overwrite (dlogits == logits) safe for the target logit too.
+  __syncthreads();
+  T* dr = dlogits + (long long)row * ld;
+  for (int c = threadIdx.x * 8; c < cols; c += kCeThreads * 8) {
+    float f[8];
+    load8_guard<T>(lr + c, f, c, cols, vec);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float p = __expf(f[i] - mx) * inv;
+      if (c + i == tgt) p -= 1.0f;
+      f[i] = p * grad_scale;
+    }
+    store8_guard<T>(dr + c, f, c, cols, vec);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads) softmax_rows_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                                  int cols) {
+  const int row = blockIdx.x;
+  const T* xr = x + (long long)row * cols;
+  T* yr = y + (long long)row * cols;
+  __shared__ float sm_m[kCeThreads / 32], sm_s[kCeThreads / 32];
+  __shared__ float row_max, row_sum;
+  float m = -INFINITY, s = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kCeThreads) online_merge(m, s, to_float<T>(xr[c]), 1.0f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sm_m[threadIdx.x >> 5] = m;
+    sm_s[threadIdx.x >> 5] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < kCeThreads / 32 ? sm_m[threadIdx.x] : -INFINITY;
+    s = threadIdx.x < kCeThreads / 32 ? sm_s[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      online_merge(m, s, m2, s2);
+    }
+    if (threadIdx.x == 0) {
+      row_max = m;
+      row_sum = s;
+    }
+  }
+  __syncthreads();
+  const float mx = row_max, inv = 1.0f / row_sum;
+  for (int c = threadIdx.x; c < cols; c += kCeThreads) yr[c] = from_float<T>(__expf(to_float<T>(xr[c]) - mx) * inv);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads) softmax_rows_bwd_kernel(const T* __restrict__ y, const T* __restrict__ dy,
+                                                                      T* __restrict__ dx, int cols) {
+  const int row = blockIdx.x;
+  const long long off = (long long)row * cols;
+  __shared__ float part[kCeThreads / 32];
+  __shared__ float dot_s;
+  float d = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kCeThreads) d += to_float<T>(y[off + c]) * to_float<T>(dy[off + c]);
+  d = warp_sum(d);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = d;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < kCeThreads / 32 ? part[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) dot_s = v;
+  }
+  __syncthreads();
+  const float dot = dot_s;
+  for (int c = threadIdx.x; c < cols; c += kCeThreads)
+    dx[off + c] = from_float<T>(to_float<T>(y[off + c]) * (to_float<T>(dy[off + c]) - dot));
+}
+
+int row_grid(int rows, int warps_per_block) {
+  long long g = (rows + warps_per_block - 1) / warps_per_block;
+  if (g > 148LL * 16) g = 148LL * 16;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+#define UHFS_DISPATCH_DTYPE(dtype, ...)                                  \
+  switch (dtype) {                                                       \
+    case DT_F32: { using T = float; __VA_ARGS__; break; }                \
+    case DT_F16: { using T = __half; __VA_ARGS__; break; }               \
+    case DT_BF16: { using T = __nv_bfloat16; __VA_ARGS__; break; }       \
+    default: throw std::runtime_error("unsupported dtype");              \
+  }
+
+void rmsnorm_fwd(int dtype, const void* x, const void* w, void* y, float* rstd, int rows, int cols, float eps,
+                 cudaStream_t s) {
+  if (rows <= 0) return;
+  const bool vec = al16(x) && al16(w) && al16(y) && (cols % 8 == 0);
+  UHFS_DISPATCH_DTYPE(dtype, rmsnorm_fwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
+                                 (const T*)x, (const T*)w, (T*)y, rstd, rows, cols, eps, vec));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const float* rstd, const void* dres,
+                 void* dx, float* dw_accum, int rows, int cols, cudaStream_t s) {
+  if (rows <= 0) return;
+  const bool vec = al16(dy) && al16(x) && al16(w) && al16(dres) && al16(dx) && (cols % 8 == 0);
+  UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dx_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
+                                 (const T*)dy, (const T*)x, (const T*)w, rstd, (const T*)dres, (T*)dx, rows, cols, vec));
+  note_launch();
+  if (dw_accum != nullptr) {
+    dim3 grid((cols + 255) / 256, (rows + 127) / 128);
+    UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dw_kernel<T><<<grid, 256, 0, s>>>((const T*)dy, (const T*)x, rstd,
+                                                                             dw_accum, rows, cols));
+    note_launch();
+  }
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_fwd(int dtype, const int64_t* ids, const void* tok, const void* pos, void* out, int rows, int dim,
+                   int seq_len, cudaStream_t s) {
+  if (rows <= 0) return;
+  const bool vec = al16(tok) && al16(pos) && al16(out) && (dim % 8 == 0);
+  UHFS_DISPATCH_DTYPE(dtype, embedding_fwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
+                                 ids, (const T*)tok, (const T*)pos, (T*)out, rows, dim, seq_len > 0 ? seq_len : 1, vec));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_bwd(int dtype, const int64_t* ids, const void* dout, float* dtok, float* dpos, int rows, int dim,
+                   int seq_len, cudaStream_t s) {
+  if (rows <= 0) return;
+  const bool vec = al16(dout) && al16(dtok) && al16(dpos) && (dim % 8 == 0);
+  UHFS_DISPATCH_DTYPE(dtype, embedding_bwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
+                                 ids, (const T*)dout, dtok, dpos, rows, dim, seq_len > 0 ? seq_len : 1, vec));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void softmax_ce_fwd_bwd(int dtype, const void* logits, long long ld, const int64_t* targets, float* loss_rows,
+                        void* dlogits, int rows, int cols, float grad_scale, const float* grad_scale_ptr,
+                        cudaStream_t s) {
+  if (rows <= 0) return;
+  const bool vec = al16(logits) && al16(dlogits) && (cols % 8 == 0) && (ld % 8 == 0);
+  UHFS_DISPATCH_DTYPE(dtype, softmax_ce_kernel<T><<<rows, kCeThreads, 0, s>>>(
+                                 (const T*)logits, ld, targets, loss_rows, (T*)dlogits, cols, grad_scale, grad_scale_ptr, vec));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void softmax_rows(int dtype, const void* x, void* y, int rows, int cols, cudaStream_t s) {
+  if (rows <= 0) return;
+  UHFS_DISPATCH_DTYPE(dtype, softmax_rows_kernel<T><<<rows, kCeThreads, 0, s>>>((const T*)x, (T*)y, cols));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void softmax_rows_bwd(int dtype, const void* y, const void* dy, void* dx, int rows, int cols, cudaStream_t s) {
+  if (rows <= 0) return;
+  UHFS_DISPATCH_DTYPE(dtype, softmax_rows_bwd_kernel<T><<<rows, kCeThreads, 0, s>>>((const T*)y, (const T*)dy,
+                                                                                     (T*)dx, cols));
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace uhfs

@@ -1,0 +1,222 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 oracle."""
+
+import math
+
+import pytest
+import torch
+
+from tests import oracles as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    from underhfs_b200.ops import kernels
+
+    torch.manual_seed(0)
+    return kernels
+
+
+def _status_ok():
+    from underhfs_b200.ops._lib import core
+
+    st = core().device_status(True)
+    assert st["code"] == 0, st
+
+
+def bf(x):
+    return x.to(torch.bfloat16)
+
+
+GEMM_SHAPES = [(128, 256, 64), (300, 264, 200), (1024, 768, 768), (2048, 2304, 768), (777, 1032, 1000)]
+
+
+@pytest.mark.parametrize("M,N,K_", GEMM_SHAPES)
+def test_gemm_forward_epilogues(K, M, N, K_):
+    dev = "cuda"
+    x = bf(torch.randn(M, K_, device=dev))
+    w = bf(torch.randn(N, K_, device=dev) / math.sqrt(K_))
+    b = bf(torch.randn(N, device=dev))
+    ref = x.float() @ w.float().t()
+    y = K.linear_fwd(x, w)
+    assert O.rel_err(y, ref) < 2e-2
+    y = K.linear_fwd(x, w, b)
+    assert O.rel_err(y, ref + b.float()) < 2e-2
+    r = bf(torch.randn(M, N, device=dev))
+    y = K.linear_fwd_resid(x, w, b, r)
+    assert O.rel_err(y, ref + b.float() + r.float()) < 2e-2
+    u, g = K.linear_fwd_gelu(x, w, b)
+    assert O.rel_err(u, ref + b.float()) < 2e-2
+    assert O.rel_err(g, O.gelu_tanh(ref + b.float())) < 2e-2
+    _status_ok()
+
+
+@pytest.mark.parametrize("M,N,K_", GEMM_SHAPES)
+def test_gemm_dgrad_wgrad(K, M, N, K_):
+    dev = "cuda"
+    dy = bf(torch.randn(M, N, device=dev))
+    w = bf(torch.randn(N, K_, device=dev) / math.sqrt(N))
+    x = bf(torch.randn(M, K_, device=dev))
+    dx = K.linear_dgrad(dy, w)
+    assert O.rel_err(dx, dy.float() @ w.float()) < 2e-2
+    u = bf(torch.randn(M, K_, device=dev))
+    dx2 = K.linear_dgrad(dy, w, gelu_in=u)
+    gu = u.float().requires_grad_(True)
+    gd = torch.autograd.grad(O.gelu_tanh(gu).sum(), gu)[0]
+    assert O.rel_err(dx2, (dy.float() @ w.float()) * gd) < 3e-2
+    dw = torch.zeros(N, K_, device=dev)
+    K.linear_wgrad_accum(dy, x, dw)
+    ref = dy.float().t() @ x.float()
+    assert O.rel_err(dw, ref) < 1e-2
+    K.linear_wgrad_accum(dy, x, dw)  # accumulates
+    assert O.rel_err(dw, 2 * ref) < 1e-2
+    _status_ok()
+
+
+def test_matmul_bf16_and_f32(K):
+    a = torch.randn(130, 72, device="cuda")
+    b = torch.randn(72, 200, device="cuda")
+    assert O.rel_err(K.matmul_bf16(bf(a), bf(b)), a @ b) < 3e-2
+    c = K.matmul_f32(a, b)
+    assert torch.allclose(c, a @ b, atol=1e-4, rtol=1e-4)
+    exact = K.matmul_f32(torch.tensor([[1.0, 2.0], [3.0, 4.0]], device="cuda"),
+                         torch.tensor([[5.0, 6.0], [7.0, 8.0]], device="cuda"))
+    assert exact.tolist() == [[19.0, 22.0], [43.0, 50.0]]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_elementwise_reduce_cast(K, dtype):
+    n = (1 << 20) + 7
+    a = torch.randn(n, device="cuda").to(dtype)
+    b = torch.randn(n, device="cuda").to(dtype)
+    for op, fn in ((K.OP_ADD, torch.add), (K.OP_MUL, torch.mul), (K.OP_SUB, torch.sub)):
+        out = K.ew_binary(op, a, b)
+        ref = fn(a.float(), b.float()).to(dtype)
+        assert torch.equal(out, ref)
+    s = K.reduce_sum(a)
+    assert abs(s.item() - a.float().sum().item()) < 1e-3 * n ** 0.5
+    c = K.cast(a, torch.float32)
+    assert torch.equal(c, a.float())
+    odd = a[1:]  # misaligned start exercises the scalar path
+    assert torch.equal(K.ew_binary(K.OP_ADD, odd.contiguous(), odd.contiguous()), (odd.float() * 2).to(dtype))
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 768), (33, 200), (4096, 2048)])
+def test_rmsnorm(K, rows, cols):
+    x = bf(torch.randn(rows, cols, device="cuda"))
+    w = bf(torch.rand(cols, device="cuda") + 0.5)
+    y, rstd = K.rmsnorm(x, w, 1e-6)
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    ref = O.rmsnorm(xf, wf, 1e-6)
+    assert O.rel_err(y, ref) < 1e-2
+    dy = bf(torch.randn(rows, cols, device="cuda"))
+    dres = bf(torch.randn(rows, cols, device="cuda"))
+    dw = torch.zeros(cols, device="cuda")
+    dx = K.rmsnorm_backward(dy, x, w, rstd, dres, dw)
+    gx, gw = torch.autograd.grad(ref, (xf, wf), dy.float())
+    assert O.rel_err(dx, gx + dres.float()) < 2e-2
+    assert O.rel_err(dw, gw) < 1e-2
+
+
+def test_embedding(K):
+    V, F, B, T = 1000, 256, 3, 17
+    tok = bf(torch.randn(V, F, device="cuda"))
+    pos = bf(torch.randn(32, F, device="cuda"))
+    ids = torch.randint(0, V, (B, T), device="cuda")
+    out = K.embedding(ids.reshape(-1), tok, pos, T)
+    ref = tok.float()[ids] + pos.float()[:T]
+    assert O.rel_err(out, ref.reshape(-1, F)) < 1e-2
+    dout = bf(torch.randn(B * T, F, device="cuda"))
+    dtok = torch.zeros(V, F, device="cuda")
+    dpos = torch.zeros(32, F, device="cuda")
+    K.embedding_backward(ids.reshape(-1), dout, dtok, dpos, T)
+    rt = torch.zeros(V, F, device="cuda").index_add_(0, ids.reshape(-1), dout.float())
+    rp = torch.zeros(32, F, device="cuda")
+    rp[:T] = dout.float().view(B, T, F).sum(0)
+    assert torch.allclose(dtok, rt, atol=1e-3)
+    assert torch.allclose(dpos, rp, atol=1e-3)
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 32000), (5, 1003)])
+def test_softmax_cross_entropy(K, rows, cols):
+    logits = bf(torch.randn(rows, cols, device="cuda") * 3)
+    tg = torch.randint(0, cols, (rows,), device="cuda")
+    lf = logits.float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(lf, tg, reduction="none")
+    dl = torch.empty_like(logits)
+    loss = K.softmax_cross_entropy(logits, tg, dl, 1.0 / rows)
+    assert torch.allclose(loss, ref, atol=2e-3, rtol=1e-3)
+    g = torch.autograd.grad(ref.mean(), lf)[0]
+    assert O.rel_err(dl, g) < 2e-2
+    scale = torch.tensor(2.0, device="cuda")
+    K.softmax_cross_entropy(logits, tg, dl, 1.0 / rows, scale)
+    assert O.rel_err(dl, 2 * g) < 2e-2
+    # in place
+    buf = logits.clone()
+    K.softmax_cross_entropy(buf, tg, buf, 1.0 / rows)
+    assert O.rel_err(buf, g) < 2e-2
+
+
+@pytest.mark.parametrize("B,T,H,D,causal", [(2, 256, 2, 64, True), (1, 200, 3, 64, True), (2, 128, 2, 64, False),
+                                            (1, 190, 2, 128, True), (2, 1024, 4, 64, True)])
+def test_flash_attention(K, B, T, H, D, causal):
+    F = H * D
+    qkv = bf(torch.randn(B * T, 3 * F, device="cuda"))
+    o, lse = K.flash_attn_qkv(qkv, B, T, H, D, causal)
+    q, k, v = (qkv.float().view(B, T, 3, H, D)[:, :, i].clone().requires_grad_(True) for i in range(3))
+    ref = O.attention(q, k, v, causal, 1.0 / math.sqrt(D))
+    assert O.rel_err(o.view(B, T, H, D), ref) < 2e-2
+    do = bf(torch.randn(B * T, F, device="cuda"))
+    dqkv = K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, causal)
+    gq, gk, gv = torch.autograd.grad(ref, (q, k, v), do.float().view(B, T, H, D))
+    d = dqkv.float().view(B, T, 3, H, D)
+    assert O.rel_err(d[:, :, 0], gq) < 3e-2
+    assert O.rel_err(d[:, :, 1], gk) < 3e-2
+    assert O.rel_err(d[:, :, 2], gv) < 3e-2
+    _status_ok()
+
+
+def test_adamw_flat(K):
+    n = 10007
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    p16 = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    rp, rm, rv = p.clone(), m.clone(), v.clone()
+    lr, b1, b2, eps, wd = 1e-2, 0.9, 0.999, 1e-8, 0.1
+    for step in (1, 2):
+        K.adamw_(p, g, m, v, p16, lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd, decoupled=False, step=step)
+        gg = g + wd * rp
+        rm = b1 * rm + (1 - b1) * gg
+        rv = b2 * rv + (1 - b2) * gg * gg
+        rp = rp - lr * (rm / (1 - b1 ** step)) / ((rv / (1 - b2 ** step)).sqrt() + eps)
+    assert torch.allclose(p, rp, atol=1e-5, rtol=1e-5)
+    assert torch.allclose(m, rm, atol=1e-6)
+    assert torch.equal(p16, p.to(torch.bfloat16))
+
+
+def test_reference_contract_kernels(K):
+    from underhfs_b200.ops._lib import core
+
+    c = core()
+    assert c.cuda_add_f32([1.0, 2.0], [3.0, 4.0]) == [4.0, 6.0]
+    r = c.cuda_fused_adamw_f32([1.0, 2.0], [0.1, 0.2], [0.0, 0.0], [0.0, 0.0], 0.01, 0.9, 0.999, 1e-8, 0.0, 1)
+    assert abs(r["m"][0] - 0.01) < 1e-6 and abs(r["m"][1] - 0.02) < 1e-6
+    a = c.cuda_attention_f32([1.0, 0.0, 0.0, 1.0], [1.0, 0.0, 0.0, 1.0], [1.0, 2.0, 3.0, 4.0], 2, 2, 1.0, False)
+    assert len(a) == 4
+    t = c.CudaTensorF32([1.0, 2.0, 3.0, 4.0], [2, 2])
+    u = c.CudaTensorF32([5.0, 6.0, 7.0, 8.0], [2, 2])
+    assert t.matmul(u).to_host() == [19.0, 22.0, 43.0, 50.0]
+    assert t.sum().to_host() == [10.0]
+    for ctor in (c.CudaTensorF16, c.CudaTensorBF16):
+        x = ctor([1.0, 2.0], [2])
+        y = ctor([3.0, 4.0], [2])
+        assert x.add(y).to_host() == [4.0, 6.0]
+        assert x.mul(y).to_host() == [3.0, 8.0]
+    assert c.cudnn_conv2d_backward_input_f32([1.0], [2.0], 1, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0) == [2.0]
+    stats = c.cuda_stream_stats()
+    assert stats["non_blocking_streams"] == 1 and stats["launches"] > 0
+    assert c.cuda_allocator_stats()["allocated_bytes"] > 0
