@@ -98,8 +98,19 @@ def _ninja_file() -> str:
         lines.append(f"build {obj}: {rule} {src}")
         objs.append(str(obj))
     lines.append(f"build {output_path()}: link {' '.join(objs)}")
-    lines.append(f"default {output_path()}")
+    # native JSON-lines server (serve.CppJsonPredictServer)
+    lines += [
+        "rule cxxexe",
+        "  command = $cxx -O2 -std=c++17 $in -o $out",
+        "  description = CXX-EXE $out",
+        f"build {serve_exe_path()}: cxxexe {CSRC / 'serve' / 'serve_main.cpp'}",
+    ]
+    lines.append(f"default {output_path()} {serve_exe_path()}")
     return "\n".join(lines) + "\n"
+
+
+def serve_exe_path() -> Path:
+    return PKG / "bin" / "underhfs_cpp_serve"
 
 
 def build(verbose: bool = False, jobs: int | None = None) -> Path:

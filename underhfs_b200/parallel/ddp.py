@@ -1,0 +1,89 @@
+"""Bucketed gradient all-reduce overlapped with backward.
+
+The engine's flat fp32 gradient buffer is re-homed into symmetric memory.
+Bucket boundaries are fixed at construction (every rank identical): equal
+``bucket_bytes`` slices counted from the END of the buffer, because backward
+completes the last blocks first.  ``on_ready(lo, hi)`` (called by the engine
+after each block) launches every bucket that is now entirely final with the
+fused two-shot all-reduce kernel on a high-priority side stream, after an
+event recorded on the compute stream.  ``finish()`` flushes the remaining
+buckets and makes the compute stream wait for the side stream, so the
+optimizer step sees reduced gradients.
+
+Reference: distributed.py:162-168 (one host-staged fp32 NCCL all-reduce per
+parameter after backward, no overlap).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from underhfs_b200.ops._lib import core
+from underhfs_b200.parallel.symmetric import SymmetricBuffer
+
+
+class BucketedAllReduce:
+    def __init__(self, model, policy, *, bucket_bytes: int, average: bool, blocks: int = 32,
+                 use_nccl: bool = False) -> None:
+        self.model = model
+        self.policy = policy
+        self.world = policy.world_size
+        self.rank = policy.rank
+        self.scale = 1.0 / self.world if average else 1.0
+        self.blocks = blocks
+        self.use_nccl = use_nccl
+        flat = model.flat
+        n = (flat.numel + 3) // 4 * 4
+        self.sym = SymmetricBuffer(n * 4, rank=self.rank, world=self.world)
+        grads = self.sym.tensor(n, torch.float32)
+        model.rehome_buffers(grads=grads)
+        self.flat = model.flat
+        self.n = n
+        per = max(4, (bucket_bytes // 4) // 4 * 4)
+        edges = list(range(n, 0, -per)) + [0]
+        self.buckets = [(edges[i + 1], edges[i]) for i in range(len(edges) - 1)]  # descending ranges
+        self.stream = torch.cuda.Stream(priority=-1)
+        self._next = 0
+        self._enabled = True
+        self._launched_any = False
+        model.engine.grad_ready = self.on_ready
+
+    def arm(self, enabled: bool = True) -> None:
+        self._next = 0
+        self._enabled = enabled
+        self._launched_any = False
+        self.model.engine.grad_ready = self.on_ready if enabled else None
+
+    def _launch(self, lo: int, hi: int) -> None:
+        compute = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(compute)
+        self.stream.wait_event(ev)
+        with torch.cuda.stream(self.stream):
+            if self.use_nccl:
+                import torch.distributed as dist
+
+                view = self.flat.grads[lo:hi]
+                dist.all_reduce(view)
+                if self.scale != 1.0:
+                    view.mul_(self.scale)
+            else:
+                core().comm_allreduce_f32(self.sym.heap, lo * 4, hi - lo, self.scale, self.blocks,
+                                          self.stream.cuda_stream)
+        self._launched_any = True
+
+    def on_ready(self, lo: int, hi: int) -> None:
+        if not self._enabled:
+            return
+        while self._next < len(self.buckets) and self.buckets[self._next][0] >= lo:
+            blo, bhi = self.buckets[self._next]
+            self._launch(blo, bhi)
+            self._next += 1
+
+    def finish(self) -> None:
+        while self._next < len(self.buckets):
+            blo, bhi = self.buckets[self._next]
+            self._launch(blo, bhi)
+            self._next += 1
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self._next = 0

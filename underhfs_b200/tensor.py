@@ -180,21 +180,22 @@ class Tensor:
             _data = t
         self._data = _data
         self.backend = _backend
-        self._prev: set = set()
+        self._prev: tuple = ()
         self._op = ""
 
     # ------------------------------------------------------------ wrapping
     @classmethod
     def _wrap(cls, t: torch.Tensor, like: "Tensor | None" = None, backend: str = "python",
-              dtype: DType | None = None) -> "Tensor":
+              dtype: DType | None = None, op: str = "", parents: tuple = ()) -> "Tensor":
         out = cls.__new__(Tensor)
         out._data = t
         out.dtype = dtype if dtype is not None else (like.dtype if like is not None else dtype_from_torch(t.dtype))
         out.device = Device.parse(t.device)
         out.layout = like.layout if like is not None else Layout.DENSE
         out.backend = backend
-        out._prev = set()
-        out._op = ""
+        # op tape used by the compile report (compile.py walks _prev like the reference)
+        out._prev = tuple(p for p in parents if isinstance(p, Tensor))
+        out._op = op
         return out
 
     # ------------------------------------------------------------ metadata
@@ -399,7 +400,8 @@ class Tensor:
             ):
                 from underhfs_b200.ops import functions as OF
 
-                return Tensor._wrap(OF.ew(op, self._data, rhs._data), like=self, backend="native_cuda")
+                return Tensor._wrap(OF.ew(op, self._data, rhs._data), like=self, backend="native_cuda", op=op,
+                                    parents=(self, rhs))
             a, b = self._data, rhs._data
             if b.dtype != a.dtype:
                 b = b.to(a.dtype)
@@ -415,7 +417,7 @@ class Tensor:
             and rhs._native_cpu_eligible()
         ):
             backend = "native_cpu"
-        return Tensor._wrap(fn(a, b), like=self, backend=backend)
+        return Tensor._wrap(fn(a, b), like=self, backend=backend, op=op, parents=(self, rhs))
 
     def __add__(self, other: Any) -> "Tensor":
         return self._binary(other, "add")
@@ -445,7 +447,7 @@ class Tensor:
         return self * -1.0
 
     def __pow__(self, power: float) -> "Tensor":
-        return Tensor._wrap(self._data ** power, like=self)
+        return Tensor._wrap(self._data ** power, like=self, op="pow", parents=(self,))
 
     def __matmul__(self, other: Any) -> "Tensor":
         rhs = self._ensure(other)
@@ -460,9 +462,10 @@ class Tensor:
         if self.device.kind == "cuda" and self.dtype in CUDA_TORCH_DTYPE:
             from underhfs_b200.ops import functions as OF
 
-            return Tensor._wrap(OF.matmul(self._data, rhs._data), like=self, backend="native_cuda")
+            return Tensor._wrap(OF.matmul(self._data, rhs._data), like=self, backend="native_cuda", op="matmul",
+                                parents=(self, rhs))
         backend = "native_cpu" if (self._native_cpu_eligible() and rhs._native_cpu_eligible()) else "python"
-        return Tensor._wrap(self._data @ rhs._data, like=self, backend=backend)
+        return Tensor._wrap(self._data @ rhs._data, like=self, backend=backend, op="matmul", parents=(self, rhs))
 
     def add_(self, other: Any) -> "Tensor":
         rhs = self._ensure(other)
@@ -485,25 +488,25 @@ class Tensor:
         if self.device.kind == "cuda" and self.dtype is DType.FP32 and self._data.is_contiguous():
             from underhfs_b200.ops import functions as OF
 
-            return Tensor._wrap(OF.sum_all(self._data), like=self, backend="native_cuda")
+            return Tensor._wrap(OF.sum_all(self._data), like=self, backend="native_cuda", op="sum", parents=(self,))
         backend = "native_cpu" if self._native_cpu_eligible() else "python"
-        return Tensor._wrap(self._data.sum(), like=self, backend=backend)
+        return Tensor._wrap(self._data.sum(), like=self, backend=backend, op="sum", parents=(self,))
 
     def mean(self) -> "Tensor":
         return self.sum() / max(1, self.numel())
 
     # ---------------------------------------------------------- unary
     def relu(self) -> "Tensor":
-        return Tensor._wrap(torch.relu(self._data), like=self)
+        return Tensor._wrap(torch.relu(self._data), like=self, op="relu", parents=(self,))
 
     def tanh(self) -> "Tensor":
-        return Tensor._wrap(torch.tanh(self._data), like=self)
+        return Tensor._wrap(torch.tanh(self._data), like=self, op="tanh", parents=(self,))
 
     def exp(self) -> "Tensor":
-        return Tensor._wrap(torch.exp(self._data), like=self)
+        return Tensor._wrap(torch.exp(self._data), like=self, op="exp", parents=(self,))
 
     def log(self) -> "Tensor":
-        return Tensor._wrap(torch.log(self._data), like=self)
+        return Tensor._wrap(torch.log(self._data), like=self, op="log", parents=(self,))
 
     def sqrt(self) -> "Tensor":
         return self ** 0.5
@@ -514,14 +517,15 @@ class Tensor:
         if self.device.kind == "cuda" and self.dtype in CUDA_TORCH_DTYPE:
             from underhfs_b200.ops import functions as OF
 
-            return Tensor._wrap(OF.softmax(self._data), like=self, backend="native_cuda")
-        return Tensor._wrap(torch.softmax(self._data, dim=-1), like=self)
+            return Tensor._wrap(OF.softmax(self._data), like=self, backend="native_cuda", op="softmax",
+                                parents=(self,))
+        return Tensor._wrap(torch.softmax(self._data, dim=-1), like=self, op="softmax", parents=(self,))
 
     # ---------------------------------------------------------- views
     def transpose(self) -> "Tensor":
         if self.ndim != 2:
             raise ValueError("transpose supports 2D tensors")
-        return Tensor._wrap(self._data.t(), like=self)
+        return Tensor._wrap(self._data.t(), like=self, op="transpose", parents=(self,))
 
     @property
     def T(self) -> "Tensor":
@@ -535,7 +539,7 @@ class Tensor:
             raise ValueError("view requires a contiguous tensor; call reshape() for a copied fallback")
         if _prod(actual) != self.numel():
             raise ValueError(f"cannot view {self.shape} as {actual}")
-        return Tensor._wrap(self._data.view(actual), like=self, backend=self.backend)
+        return Tensor._wrap(self._data.view(actual), like=self, backend=self.backend, op="view", parents=(self,))
 
     def flatten(self) -> "Tensor":
         return self.view(self.numel())
@@ -548,7 +552,7 @@ class Tensor:
             raise ValueError(f"cannot reshape {self.shape} to {actual}")
         if self._data.is_contiguous():
             return self.view(*actual)
-        return Tensor._wrap(self._data.reshape(actual), like=self)
+        return Tensor._wrap(self._data.reshape(actual), like=self, op="reshape", parents=(self,))
 
     def __getitem__(self, key: Any) -> "Tensor":
         if not isinstance(key, tuple):
@@ -565,7 +569,7 @@ class Tensor:
                     raise IndexError(f"index {item} is out of bounds for axis {axis} with size {dim}")
             elif not isinstance(item, slice):
                 raise IndexError("tensor indices must be integers or slices")
-        return Tensor._wrap(self._data[key], like=self)
+        return Tensor._wrap(self._data[key], like=self, op="slice", parents=(self,))
 
     def __len__(self) -> int:
         return self.shape[0] if self.shape else 0

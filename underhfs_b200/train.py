@@ -1,0 +1,135 @@
+"""Training loop front-end: model presets and the ``Trainer``.
+
+A ``Trainer`` owns one TransformerLM on the fused CUDA engine, its optimizer
+(FusedAdamW, or ZeRO-partitioned AdamW) and, for several GPUs, the
+data-parallel wrapper.  ``step(ids, targets)`` runs zero-grad, forward with
+the fused loss, backward with bucketed gradient all-reduce overlapped, and
+the optimizer update.  With ``cuda_graph=True`` the whole step is captured
+once into a CUDA graph and every later step is one graph launch fed through
+static input buffers; ``step_from_host`` adds the pinned host->device copy of
+the batch and returns the loss to the host, which is the end-to-end path a
+user drives.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from underhfs_b200.models.transformer import LMSpec
+
+PRESETS: dict[str, LMSpec] = {
+    # reference-scale byte LM (CPU path, d_model 64, 2 blocks, 4 heads)
+    "tiny": LMSpec(256, 64, 64, 256, 2, heads=4, tied=False),
+    "125m": LMSpec(32000, 1024, 768, 3072, 12, heads=12, tied=True),
+    "1.3b": LMSpec(32000, 2048, 2048, 8192, 24, heads=16, tied=True),
+    "7b": LMSpec(32000, 4096, 4096, 11008, 32, heads=32, tied=False),
+}
+
+
+@dataclass
+class TrainConfig:
+    model: str = "125m"
+    batch: int = 16
+    seq_len: int = 1024
+    lr: float = 3e-4
+    betas: tuple[float, float] = (0.9, 0.95)
+    eps: float = 1e-8
+    weight_decay: float = 0.0
+    decoupled: bool = True
+    zero_stage: int = 0
+    bucket_mb: float = 25.0
+    cuda_graph: bool = True
+    seed: int = 0
+    init: str = "normal"
+
+
+def build_model(cfg: TrainConfig, device: str = "cuda"):
+    from underhfs_b200.nn import TransformerLM
+
+    spec = PRESETS[cfg.model]
+    model = TransformerLM(spec.vocab_size, spec.max_seq_len, spec.features, spec.hidden_features, spec.layers,
+                          heads=spec.heads, tied=spec.tied, init=cfg.init, seed=cfg.seed, eps=1e-6)
+    if device.startswith("cuda"):
+        model.to(device, dtype="bf16")
+    return model
+
+
+class Trainer:
+    def __init__(self, model, cfg: TrainConfig, *, policy=None) -> None:
+        from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
+        from underhfs_b200.optim import FusedAdamW, ZeroAwareAdamW, ZeroShard
+
+        self.model = model
+        self.cfg = cfg
+        self.policy = policy or policy_from_env(bucket_mb=cfg.bucket_mb, zero_stage=cfg.zero_stage)
+        self.world = self.policy.world_size
+        self.ddp = None
+        if self.world > 1 and cfg.zero_stage == 0:
+            self.ddp = DistributedDataParallel(model, self.policy, bucket_mb=cfg.bucket_mb)
+        if cfg.zero_stage > 0:
+            if self.world > 1:
+                from underhfs_b200.distributed import init_process_group
+
+                init_process_group(self.policy)
+            self.opt = ZeroAwareAdamW(model.parameters(), ZeroShard(self.policy.rank, self.world),
+                                      stage=cfg.zero_stage, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                      weight_decay=cfg.weight_decay, decoupled=cfg.decoupled)
+        else:
+            self.opt = FusedAdamW(model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                  weight_decay=cfg.weight_decay, decoupled=cfg.decoupled)
+        dev = model.flat.device
+        self.static_ids = torch.zeros((cfg.batch, cfg.seq_len), dtype=torch.int64, device=dev)
+        self.static_tg = torch.zeros_like(self.static_ids)
+        self.static_batch = torch.zeros((2, cfg.batch, cfg.seq_len), dtype=torch.int64, device=dev)
+        self._graph = None
+        self._graph_loss = None
+        self.steps_done = 0
+
+    def _eager_step(self, ids: torch.Tensor, tg: torch.Tensor) -> torch.Tensor:
+        self.model.zero_grad()
+        runner = self.ddp if self.ddp is not None else self.model
+        loss = runner(ids, tg)
+        loss.backward()
+        if self.ddp is not None:
+            self.ddp.synchronize_gradients()
+        self.opt.step()
+        return loss._data if hasattr(loss, "_data") else loss
+
+    def _capture(self) -> None:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):  # warm-up: kernel attributes, allocator pool, workspaces
+                self._eager_step(self.static_batch[0], self.static_batch[1])
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._graph_loss = self._eager_step(self.static_batch[0], self.static_batch[1])
+        self._graph = g
+
+    def step(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on device-resident ids/targets [B, T]; returns the device loss."""
+        self.steps_done += 1
+        if not self.cfg.cuda_graph:
+            return self._eager_step(ids, targets)
+        if ids.data_ptr() != self.static_batch[0].data_ptr():
+            self.static_batch[0].copy_(ids, non_blocking=True)
+            self.static_batch[1].copy_(targets, non_blocking=True)
+        if self._graph is None:
+            self._capture()
+        self._graph.replay()
+        return self._graph_loss
+
+    def step_from_host(self, host_batch: torch.Tensor) -> float:
+        """End-to-end step: pinned host [2, B, T] int64 batch in, host float loss out."""
+        self.static_batch.copy_(host_batch, non_blocking=True)
+        loss = self.step(self.static_batch[0], self.static_batch[1])
+        return float(loss.item())
+
+    def release(self) -> None:
+        """Drop the captured graph (before destroying the process group)."""
+        self._graph = None
+        self._graph_loss = None
