@@ -343,5 +343,11 @@ PYBIND11_MODULE(_core, m) {
         flash_attn_bwd(p, S(s));
       });
 
+  m.def("raster_iso", [](uintptr_t quads, uintptr_t colors, int n, uintptr_t order, uintptr_t rgba, int w, int h,
+                         uintptr_t s) {
+    raster_iso(P<const float>(quads), P<const unsigned int>(colors), n, P<unsigned int>(order),
+               P<unsigned int>(rgba), w, h, S(s));
+  });
+
   bind_comm(m);
 }

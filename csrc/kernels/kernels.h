@@ -108,4 +108,8 @@ struct AttnBwdParams {
 void flash_attn_fwd(const AttnParams& p, cudaStream_t s);
 void flash_attn_bwd(const AttnBwdParams& p, cudaStream_t s);
 
+// ---- headless isometric voxel rasteriser (liveSee): quads [n][8] float, colors RGBA8
+void raster_iso(const float* quads, const unsigned int* colors, int nquads, unsigned int* order, unsigned int* rgba,
+                int width, int height, cudaStream_t s);
+
 }  // namespace uhfs

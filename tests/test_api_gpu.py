@@ -147,3 +147,29 @@ def test_trainer_cuda_graph_matches_eager():
     for a, b in zip(out[False], out[True]):
         assert abs(a - b) < 2e-2 * max(1.0, abs(a)), out
     assert out[True][-1] < out[True][0]
+
+
+def test_livesee_gpu_raster_matches_cpu_oracle():
+    _cuda()
+    import importlib.util
+    import sys
+    from pathlib import Path
+
+    import numpy as np
+
+    root = Path(__file__).resolve().parents[1] / "project" / "liveSee"
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root.parent))
+    mods = {}
+    for name in ("raster", "play_live_world"):
+        spec = importlib.util.spec_from_file_location(name, root / f"{name}.py")
+        mods[name] = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mods[name]
+        spec.loader.exec_module(mods[name])
+    chunk = mods["play_live_world"].LiveWorldSession(steps=1).state()
+    gpu = mods["raster"].render_frame(chunk, 480, 270)
+    cpu = mods["raster"].render_frame_cpu(chunk, 480, 270)
+    diff = np.zeros(gpu.shape, dtype=np.int64)
+    for s in (0, 8, 16):
+        diff = np.maximum(diff, np.abs(((gpu >> s) & 255).astype(np.int64) - ((cpu >> s) & 255).astype(np.int64)))
+    assert (diff == 0).mean() > 0.995 and diff.max() <= 1 or (diff == 0).mean() > 0.999

@@ -97,11 +97,29 @@ class Trainer:
         self.opt.step()
         return loss._data if hasattr(loss, "_data") else loss
 
+    def _state_tensors(self) -> list[torch.Tensor]:
+        """Every tensor a training step mutates (weights, master, moments, step counters)."""
+        f = self.model.flat
+        out = [f.params]
+        if f.master is not None:
+            out.append(f.master)
+        for name in ("_m_flat", "_v_flat", "_step_t"):
+            t = getattr(self.opt, name, None)
+            if isinstance(t, torch.Tensor):
+                out.append(t)
+        z = getattr(self.opt, "_zero", None)
+        if z is not None:
+            out += [z.master, z.m, z.v, z.step_t]
+        return out
+
     def _capture(self) -> None:
+        # warm-up steps (kernel attributes, allocator pool, workspaces) must not
+        # change the training trajectory: snapshot and restore the state
+        saved = [t.detach().clone() for t in self._state_tensors()]
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            for _ in range(2):  # warm-up: kernel attributes, allocator pool, workspaces
+            for _ in range(2):
                 self._eager_step(self.static_batch[0], self.static_batch[1])
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
@@ -109,6 +127,9 @@ class Trainer:
         with torch.cuda.graph(g):
             self._graph_loss = self._eager_step(self.static_batch[0], self.static_batch[1])
         self._graph = g
+        for t, s in zip(self._state_tensors(), saved):
+            t.copy_(s)
+        torch.cuda.synchronize()
 
     def step(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One optimizer step on device-resident ids/targets [B, T]; returns the device loss."""
