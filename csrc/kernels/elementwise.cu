@@ -178,7 +178,46 @@ __global__ void __launch_bounds__(kReduceThreads) reduce_sum_kernel(const T* __r
   }
 }
 
-// db[c] += sum_r x[r, c]; 128 threads x 2 columns, 256 rows per block-row.
+// out[c] += sum_r x[r, c] for bf16 x with cols % 8 == 0 and 16-byte rows.
+// A warp owns 256 consecutive columns (8 per lane, one 16-byte load per row),
+// the 8 warps of a block stride over the block's rows, partial sums are
+// combined in shared memory and added to `out` with one atomic per column per
+// block.  Every warp load is a contiguous 512-byte segment.
+__global__ void __launch_bounds__(256) colsum_vec_kernel(const __nv_bfloat16* __restrict__ x, long long ld,
+                                                         float* __restrict__ out, int rows, int cols,
+                                                         int rows_per_block) {
+  __shared__ float part[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < cols) {
+#pragma unroll 4
+    for (int r = r0 + warp; r < r1; r += 8) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (long long)r * ld + c0));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < cols) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w][threadIdx.x];
+    atomicAdd(out + c, s);
+  }
+}
+
+// db[c] += sum_r x[r, c]; 128 threads x 2 columns, 256 rows per block-row (any alignment).
 __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, long long ld, float* __restrict__ out, int rows,
                               int cols) {
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
@@ -335,8 +374,17 @@ void gelu_bwd(int dtype, const void* x, const void* dy, void* dx, long long n, c
 
 void colsum_accum(const __nv_bfloat16* x, long long ld, float* out, int rows, int cols, cudaStream_t s) {
   if (rows <= 0 || cols <= 0) return;
-  dim3 grid((cols / 2 + 127) / 128 + 1, (rows + 255) / 256);
-  colsum_kernel<<<grid, 128, 0, s>>>(x, ld, out, rows, cols);
+  if (cols % 8 == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const int gx = (cols + 255) / 256;
+    int gy = (2 * 148 + gx - 1) / gx;
+    int rpb = (rows + gy - 1) / gy;
+    rpb = (rpb + 7) / 8 * 8;
+    gy = (rows + rpb - 1) / rpb;
+    colsum_vec_kernel<<<dim3(gx, gy), 256, 0, s>>>(x, ld, out, rows, cols, rpb);
+  } else {
+    dim3 grid((cols / 2 + 127) / 128 + 1, (rows + 255) / 256);
+    colsum_kernel<<<grid, 128, 0, s>>>(x, ld, out, rows, cols);
+  }
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

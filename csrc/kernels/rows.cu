@@ -87,6 +87,43 @@ __global__ void rmsnorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __restr
   }
 }
 
+// dw_j += sum_rows dy_rj * x_rj * r_r, 16-byte vector form: a warp owns 256
+// columns (8 per lane), 8 warps stride over the block's rows, shared-memory
+// combine, one atomic per column per block.
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_dw_vec_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                                 const float* __restrict__ rstd,
+                                                                 float* __restrict__ dw, int rows, int cols,
+                                                                 int rows_per_block) {
+  __shared__ float part[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < cols) {
+#pragma unroll 2
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float a[8], b[8];
+      load8<T>(dy + (long long)r * cols + c0, a);
+      load8<T>(x + (long long)r * cols + c0, b);
+      const float rs = rstd[r];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += a[j] * b[j] * rs;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < cols) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w][threadIdx.x];
+    atomicAdd(dw + c, s);
+  }
+}
+
 // dw_j += sum_rows dy_rj * x_rj * r_r; one thread per column pair-of-4, 128 rows per block-row.
 template <typename T>
 __global__ void rmsnorm_bwd_dw_kernel(const T* __restrict__ dy, const T* __restrict__ x,
@@ -347,9 +384,19 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
                                  (const T*)dy, (const T*)x, (const T*)w, rstd, (const T*)dres, (T*)dx, rows, cols, vec));
   note_launch();
   if (dw_accum != nullptr) {
-    dim3 grid((cols + 255) / 256, (rows + 127) / 128);
-    UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dw_kernel<T><<<grid, 256, 0, s>>>((const T*)dy, (const T*)x, rstd,
-                                                                             dw_accum, rows, cols));
+    if (vec) {
+      const int gx = (cols + 255) / 256;
+      int gy = (2 * 148 + gx - 1) / gx;
+      int rpb = (rows + gy - 1) / gy;
+      rpb = (rpb + 7) / 8 * 8;
+      gy = (rows + rpb - 1) / rpb;
+      UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dw_vec_kernel<T><<<dim3(gx, gy), 256, 0, s>>>(
+                                     (const T*)dy, (const T*)x, rstd, dw_accum, rows, cols, rpb));
+    } else {
+      dim3 grid((cols + 255) / 256, (rows + 127) / 128);
+      UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dw_kernel<T><<<grid, 256, 0, s>>>((const T*)dy, (const T*)x, rstd,
+                                                                               dw_accum, rows, cols));
+    }
     note_launch();
   }
   UHFS_CUDA_CHECK(cudaGetLastError());

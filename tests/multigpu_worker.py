@@ -1,0 +1,143 @@
+"""Worker for tests/test_multigpu.py (one process per GPU, launched by torchrun).
+
+    python -m torch.distributed.run --nproc-per-node 2 tests/multigpu_worker.py {allreduce|ddp|zero}
+
+Exits 0 and prints "OK <case>" on rank 0 when the fused NVLink kernels agree
+with NCCL / the single-buffer reference; any mismatch raises.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+
+def _setup():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    return rank, world
+
+
+def case_allreduce(rank: int, world: int) -> None:
+    from underhfs_b200.ops._lib import core
+    from underhfs_b200.parallel.symmetric import SymmetricBuffer
+
+    sym = SymmetricBuffer(64 << 20, rank=rank, world=world)
+    buf = sym.tensor((64 << 20) // 4 - 1024, torch.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+    for n in (4, 1000, 4096 * 1024 + 4, (25 << 20) // 4, (64 << 20) // 4 - 1024):
+        gen = torch.Generator(device="cuda").manual_seed(1000 + rank * 7 + n % 97)
+        x = torch.randn(n, device="cuda", generator=gen)
+        buf[:n].copy_(x)
+        ref = x.clone()
+        dist.all_reduce(ref)
+        ref /= world
+        off = buf.data_ptr() - sym.heap.data_ptr(rank)
+        for blocks in (8, 64):
+            buf[:n].copy_(x)
+            core().comm_allreduce_f32(sym.heap, off, n, 1.0 / world, blocks, stream)
+            torch.cuda.synchronize()
+            err = (buf[:n] - ref).abs().max().item()
+            assert err < 1e-5 * max(1.0, ref.abs().max().item()), (n, blocks, err)
+    st = core().device_status(True)
+    assert st["code"] == 0, st
+
+
+def _model(seed: int = 0):
+    from underhfs_b200.nn import TransformerLM
+
+    m = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=2, heads=4,
+                      tied=True, init="normal", seed=seed)
+    m.to(f"cuda:{torch.cuda.current_device()}", dtype="bf16")
+    return m
+
+
+def case_ddp(rank: int, world: int) -> None:
+    from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
+
+    gen = torch.Generator().manual_seed(100 + rank)
+    ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+    tg = torch.roll(ids, -1, 1)
+    ref_model = _model()
+    ref_model.zero_grad()
+    ref_model(ids, tg).backward()
+    ref = ref_model.flat.grads.clone()
+    dist.all_reduce(ref)
+    ref /= world
+    model = _model()
+    ddp = DistributedDataParallel(model, policy_from_env(), bucket_mb=0.25)  # small buckets: many overlap launches
+    for _ in range(2):  # second pass checks the epochs of reused buckets
+        model.zero_grad()
+        ddp(ids, tg).backward()
+        ddp.synchronize_gradients()
+        torch.cuda.synchronize()
+        err = ((model.flat.grads - ref).abs().max() / ref.abs().max()).item()
+        assert err < 1e-4, err
+    with ddp.no_sync():
+        model.zero_grad()
+        ddp(ids, tg).backward()
+        ddp.synchronize_gradients()
+    torch.cuda.synchronize()
+    local = ((model.flat.grads - ref_model.flat.grads).abs().max() / ref_model.flat.grads.abs().max()).item()
+    assert local < 1e-4, local  # no_sync keeps local gradients
+    from underhfs_b200.ops._lib import core
+
+    assert core().device_status(True)["code"] == 0
+
+
+def case_zero(rank: int, world: int) -> None:
+    from underhfs_b200.optim import FusedAdamW, ZeroAwareAdamW, ZeroShard
+
+    gen = torch.Generator().manual_seed(200 + rank)
+    ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+    tg = torch.roll(ids, -1, 1)
+    kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, decoupled=True)
+    ref_model = _model()
+    ref_opt = FusedAdamW(ref_model.parameters(), **kw)
+    model = _model()
+    opt = ZeroAwareAdamW(model.parameters(), ZeroShard(rank, world), stage=2, **kw)
+    for _ in range(3):
+        ref_model.zero_grad()
+        ref_model(ids, tg).backward()
+        dist.all_reduce(ref_model.flat.grads)
+        ref_model.flat.grads /= world
+        ref_opt.step()
+        model.zero_grad()
+        model(ids, tg).backward()
+        opt.step()
+        torch.cuda.synchronize()
+        a = model.flat.params.float()
+        b = ref_model.flat.params.float()
+        err = ((a - b).abs().max() / b.abs().max()).item()
+        assert err < 2e-2, err
+    # every rank holds identical full parameters after the fused all-gather
+    p = model.flat.params.float().sum().reshape(1)
+    allp = [torch.zeros_like(p) for _ in range(world)]
+    dist.all_gather(allp, p)
+    assert all(torch.equal(allp[0], q) for q in allp)
+
+
+def main() -> int:
+    case = sys.argv[1]
+    rank, world = _setup()
+    try:
+        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero}[case](rank, world)
+        dist.barrier()
+        if rank == 0:
+            print(f"OK {case}", flush=True)
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,34 @@
+"""Two-GPU correctness of the fused collectives, DDP overlap and ZeRO-2.
+
+Each case runs tests/multigpu_worker.py under torchrun with one process per
+GPU; the worker compares against NCCL / single-buffer references.
+"""
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero"])
+def test_two_gpu_case(case):
+    env = dict(os.environ)
+    env["PYTHONPATH"] = str(ROOT) + os.pathsep + env.get("PYTHONPATH", "")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           str(ROOT / "tests" / "multigpu_worker.py"), case]
+    proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    assert proc.returncode == 0 and f"OK {case}" in proc.stdout, (proc.stdout[-3000:], proc.stderr[-6000:])
