@@ -9,7 +9,9 @@
 // swizzled shared memory, memory O(T).  Q/K/V/O are addressed as [B, T, H, D]
 // rows with arbitrary batch/token strides, so the fused QKV projection output
 // [B*T, 3*H*D] is consumed in place.
+#include <cstdlib>
 #include <stdexcept>
+#include <string>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -507,9 +509,17 @@ void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
   if (g1 > 148 * 16) g1 = 148 * 16;
   fa_bwd_prep_kernel<D><<<g1, 256, 0, s>>>(p);
   note_launch();
-  dim3 grid((p.f.T + 63) / 64, p.f.B * p.f.H);
-  fa_bwd_kernel<D><<<grid, 128, smem, s>>>(p);
-  note_launch();
+  static const bool legacy = [] {
+    const char* e = getenv("UHFS_ATTN_BWD");
+    return e != nullptr && std::string(e) == "mma_sync";
+  }();
+  if (!legacy && flash_attn_bwd_tc_supported(p)) {
+    flash_attn_bwd_tc_main(p, s);
+  } else {
+    dim3 grid((p.f.T + 63) / 64, p.f.B * p.f.H);
+    fa_bwd_kernel<D><<<grid, 128, smem, s>>>(p);
+    note_launch();
+  }
   long long tot = rows * (D / 2);
   int g2 = (int)((tot + 255) / 256);
   if (g2 > 148 * 16) g2 = 148 * 16;
@@ -521,6 +531,14 @@ void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
 
 void flash_attn_fwd(const AttnParams& p, cudaStream_t s) {
   if (p.T <= 0 || p.B <= 0 || p.H <= 0) return;
+  static const bool use_tc = [] {
+    const char* e = getenv("UHFS_ATTN_FWD");
+    return e != nullptr && std::string(e) == "tc";
+  }();
+  if (use_tc && flash_attn_fwd_tc_supported(p)) {
+    flash_attn_fwd_tc(p, s);
+    return;
+  }
   if (p.D == 64) fwd_impl<64>(p, s);
   else if (p.D == 128) fwd_impl<128>(p, s);
   else throw std::runtime_error("flash attention supports head_dim 64 or 128");

@@ -131,6 +131,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Bounded wait called by all 32 lanes of a warp; the result is the same in
+// every lane (false if the wait gave up in any lane).  Warps that go on to
+// warp-collective tcgen05 instructions (.sync.aligned) use it so that a
+// timeout in some lanes cannot leave a partial warp at such an instruction.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, DeviceStatus* st, int err,
+                                               int where) {
+  const bool ok = mbar_wait_bounded(bar, parity, st, err, where);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled, non-multicast).  `coord0` is the innermost coordinate and must
 // be a multiple of 16 bytes / element size; callers guarantee that by tiling

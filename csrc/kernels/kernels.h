@@ -106,7 +106,14 @@ struct AttnBwdParams {
   float* dq_accum;   // [B, T, H, D] fp32 scratch (zeroed by the launcher's prologue kernel)
 };
 void flash_attn_fwd(const AttnParams& p, cudaStream_t s);
+// tcgen05/TMEM forward for the fused-QKV layout (attention_tc.cu)
+bool flash_attn_fwd_tc_supported(const AttnParams& p);
+void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s);
 void flash_attn_bwd(const AttnBwdParams& p, cudaStream_t s);
+// tcgen05/TMEM main backward kernel (attention_tc_bwd.cu); flash_attn_bwd runs the
+// delta / dQ-zeroing prologue and the dQ conversion around it
+bool flash_attn_bwd_tc_supported(const AttnBwdParams& p);
+void flash_attn_bwd_tc_main(const AttnBwdParams& p, cudaStream_t s);
 
 // ---- headless isometric voxel rasteriser (liveSee): quads [n][8] float, colors RGBA8
 void raster_iso(const float* quads, const unsigned int* colors, int nquads, unsigned int* order, unsigned int* rgba,

@@ -160,7 +160,8 @@ def test_softmax_cross_entropy(K, rows, cols):
 
 
 @pytest.mark.parametrize("B,T,H,D,causal", [(2, 256, 2, 64, True), (1, 200, 3, 64, True), (2, 128, 2, 64, False),
-                                            (1, 190, 2, 128, True), (2, 1024, 4, 64, True)])
+                                            (1, 190, 2, 128, True), (2, 1024, 4, 64, True), (1, 300, 2, 64, False),
+                                            (2, 640, 2, 128, True), (1, 333, 2, 128, False)])
 def test_flash_attention(K, B, T, H, D, causal):
     F = H * D
     qkv = bf(torch.randn(B * T, 3 * F, device="cuda"))
