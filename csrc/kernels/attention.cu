@@ -531,11 +531,11 @@ void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
 
 void flash_attn_fwd(const AttnParams& p, cudaStream_t s) {
   if (p.T <= 0 || p.B <= 0 || p.H <= 0) return;
-  static const bool use_tc = [] {
+  static const bool legacy = [] {
     const char* e = getenv("UHFS_ATTN_FWD");
-    return e != nullptr && std::string(e) == "tc";
+    return e != nullptr && std::string(e) == "mma_sync";
   }();
-  if (use_tc && flash_attn_fwd_tc_supported(p)) {
+  if (!legacy && flash_attn_fwd_tc_supported(p)) {
     flash_attn_fwd_tc(p, s);
     return;
   }

@@ -1,22 +1,34 @@
 // Flash-attention forward on the 5th-generation tensor core (tcgen05 + TMEM).
 //
-// One CTA computes 128 query rows of one (batch, head) and walks the key /
-// value sequence in blocks of 128 (causal: up to the diagonal).
+// One CTA owns 256 query rows of one (batch, head) as two 128-row tiles A and
+// B, and walks the key / value sequence in blocks of 128 (causal: up to the
+// diagonal; tile B has one block more than tile A).
 //
-//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
-//               (128B-swizzled, no multicast)
-//   warp 1      TMEM allocator + MMA issuer (one elected thread):
-//                 S_j   = Q K_j^T   (M=128, N=128, K=D)      -> TMEM S[j%2]
-//                 O_j   = P_j V_j   (M=128, N=D,   K=128)    -> TMEM O[j%2]
-//   warps 2..5  softmax: thread r owns query row r (= TMEM lane r); it reads
-//               its S row from TMEM, keeps the running max / sum and the
-//               output accumulator in registers (exp2 domain), writes P_j as
-//               bf16 into a swizzled shared tile (the A operand of the PV MMA)
-//               and folds O_j into its accumulator with the online-softmax
-//               rescale.  Finally O / l and the log2-domain LSE are stored.
+//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B (below)
+//   warp 8      TMA producer: Q_A, Q_B once; then K_0, V_0, K_1, V_1, ...
+//               through a ring of 128 x D slots (128B-swizzled, no multicast)
+//   warp 9      TMEM allocator + MMA issuer (one elected thread), ordering
+//                 S_A(j) | PV_B(j-1) | S_B(j) | PV_A(j)
+//               so the tensor core works on one tile while the softmax
+//               warpgroup of the other tile runs:
+//                 S_t(j)  = Q_t K_j^T   (M=128, N=128, K=D)   -> TMEM S_t
+//                 O_t    += P_t(j) V_j  (M=128, N=D,   K=128) -> TMEM O_t
+//   softmax     thread r of a softmax warpgroup owns query row r of its
+//               tile (= TMEM lane r; warp w reads lanes 32*(w%4)..+31).  It loads its whole S row
+//               (128 columns) with four TMEM loads and one wait, frees S for
+//               the next block, and computes P = exp2(S*scale*log2e - m) in
+//               registers.  The running max m is only raised when the block
+//               max exceeds it by more than kRescaleThreshold (log2 units);
+//               then, and only then, O in TMEM is rescaled by that warp before
+//               the next PV product.  P goes to a 128B-swizzled shared tile
+//               (the A operand of PV).  At the end O / l and the log2-domain
+//               LSE are written.
 //
-// S and O are double-buffered in TMEM, P in shared memory, so the MMA of
-// block j+1 overlaps the softmax of block j.  Every mbarrier wait is bounded.
+// Registers: 384 threads launch with 168 each; warpgroup 2 (producer, MMA,
+// two idle warps) gives back down to 96 and the softmax warpgroups take 200,
+// within the launch total (the host checks the launch count).
+// Every mbarrier wait is bounded; waits that precede warp-collective TMEM
+// instructions return a warp-uniform result.
 // Reference: the single-head fp32 kernel cuda/kernels.cu:147-188 and the
 // Python attention of nn.py:229-271.
 #include <cudaTypedefs.h>
@@ -34,27 +46,31 @@ CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, 
 
 namespace {
 
-constexpr int BQ = 128;   // query rows per CTA
+constexpr int BQ = 128;   // query rows per tile (two tiles per CTA)
 constexpr int BKV = 128;  // keys per block
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;       // 3 warpgroups
+constexpr int kLaunchRegs = 168;    // 65536 / 384, rounded down to 8
+constexpr int kSoftmaxRegs = 200;
+constexpr int kServiceRegs = 96;    // 2 * 128 * 200 + 128 * 96 <= 384 * 168
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kServiceRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
+// P = exp2(s - m) stays below 2^kRescaleThreshold when m is kept stale.
+constexpr float kRescaleThreshold = 8.0f;
 
 template <int D>
-struct FaCfg {
-  static constexpr int kQBytes = BQ * D * 2;
-  static constexpr int kKBytes = BKV * D * 2;
-  static constexpr int kVBytes = BKV * D * 2;
-  static constexpr int kPBytes = BQ * BKV * 2;
-  static constexpr int kStageBytes = kKBytes + kVBytes;
-  static constexpr int kPBuffers = (D == 64) ? 2 : 1;
-  static constexpr int kSmem = 1024 + kQBytes + 2 * kStageBytes + kPBuffers * kPBytes + 256;
-  static constexpr uint32_t kSCol = 0;            // S[2]: columns [0, 256)
-  static constexpr uint32_t kOCol = 2 * BKV;      // O[2]: columns [256, 256 + 2D)
+struct FwdCfg {
+  static constexpr int kTile = 128 * D * 2;            // one 128 x D bf16 tile (D/64 swizzled sub-tiles)
+  static constexpr int kSlots = (D == 64) ? 4 : 3;      // K / V ring
+  static constexpr int kPBytes = BQ * BKV * 2;          // P tile (2 sub-tiles of 128 x 64)
+  static constexpr int kBars = 1 + 2 * kSlots + 2 * 4 + 1;
+  static constexpr int kSmem = 1024 + 2 * kTile + kSlots * kTile + 2 * kPBytes + kBars * 8 + 16;
+  static constexpr uint32_t kSCol = 0;                  // S_A [0,128), S_B [128,256)
+  static constexpr uint32_t kOCol = 2 * BKV;            // O_A, O_B: D columns each
   static constexpr uint32_t kTmemCols = 512;
 };
 
-struct FaTcArgs {
-  int B, H, T, D;
+struct FwdArgs {
+  int H, T;
   long long F;            // H * D (columns per q / k / v section)
   float sl2;              // softmax scale * log2(e)
   int causal;
@@ -64,58 +80,58 @@ struct FaTcArgs {
   DeviceStatus* status;
 };
 
-// 32 TMEM columns of this thread's lane.
-__device__ __forceinline__ void tld32(uint32_t taddr, float* v) { tmem_ld_32x32b_x32(taddr, v); }
-
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
-    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FaTcArgs a) {
-  using Cfg = FaCfg<D>;
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FwdArgs a) {
+  using Cfg = FwdCfg<D>;
   constexpr int KD = D / 64;  // 64-column sub-tiles along the head dim
+  constexpr int NS = Cfg::kSlots;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + Cfg::kQBytes;                      // [2 stages][K | V]
-  uint8_t* sP = sKV + 2 * Cfg::kStageBytes;              // [kPBuffers][2 sub-tiles of 128 x 64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::kPBuffers * Cfg::kPBytes);
+  uint8_t* smem = smem_align1024(smem_raw);
+  uint8_t* sQ = smem;                               // [2 tiles]
+  uint8_t* sRing = sQ + 2 * Cfg::kTile;             // [NS slots]
+  uint8_t* sP = sRing + NS * Cfg::kTile;            // [2 tiles]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_free = bars + 7;    // [2]
-  uint64_t* p_full = bars + 9;    // [2]
-  uint64_t* o_full = bars + 11;   // [2]
-  uint64_t* o_free = bars + 13;   // [2]
-  uint64_t* done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* slot_full = bars + 1;
+  uint64_t* slot_empty = slot_full + NS;
+  uint64_t* s_full = slot_empty + NS;  // [2]
+  uint64_t* s_free = s_full + 2;       // [2]
+  uint64_t* p_full = s_free + 2;       // [2]
+  uint64_t* o_done = p_full + 2;       // [2]
+  uint64_t* done = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
   const int b = bh / a.H, h = bh % a.H;
   const int m_block = gridDim.x - 1 - blockIdx.x;  // longest (causal) rows first
-  const int m0 = m_block * BQ;
+  const int m0 = m_block * (2 * BQ);
   const int T = a.T;
-  const int n_end = a.causal ? min(T, m0 + BQ) : T;
-  const int nblocks = (n_end + BKV - 1) / BKV;
+  const int kv_blocks = (T + BKV - 1) / BKV;
+  const int nA = a.causal ? min(kv_blocks, m0 / BKV + 1) : kv_blocks;
+  const int nB = a.causal ? min(kv_blocks, m0 / BKV + 2) : kv_blocks;
   const int row0 = b * T;  // first row of this batch in the [B*T, 3F] matrix
 
-  if (warp == 0 && lane == 0) {
+  constexpr int kProducerWarp = 8, kMmaWarp = 9;
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&slot_full[i], 1);
+      mbar_init(&slot_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
+      mbar_init(&o_done[i], 1);
     }
     mbar_init(done, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -124,212 +140,230 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= 8) {
+    // register counts are set at the top of each role's branch so the
+    // compiler allocates every region with the count it runs under
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kServiceRegs));
+  }
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
-      mbar_arrive_expect_tx(q_full, Cfg::kQBytes);
-      for (int kd = 0; kd < KD; ++kd)
-        tma_load_2d(sQ + kd * (BQ * 128), &tm_qkv, q_full, (int)(h * D + kd * 64), row0 + m0);
-      uint32_t issued_phase[2] = {0, 0};
-      bool issued[2] = {false, false};
-      bool ok = true;
-      for (int j = 0; j < nblocks && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(&kv_empty[st], ph ^ 1u, a.status, kErrWaitTimeoutEmpty, 200)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sK = sKV + st * Cfg::kStageBytes;
-        uint8_t* sV = sK + Cfg::kKBytes;
-        mbar_arrive_expect_tx(&kv_full[st], Cfg::kStageBytes);
-        const int r = row0 + j * BKV;
-        for (int kd = 0; kd < KD; ++kd) {
-          tma_load_2d(sK + kd * (BKV * 128), &tm_qkv, &kv_full[st], (int)(a.F + h * D + kd * 64), r);
-          tma_load_2d(sV + kd * (BKV * 128), &tm_qkv, &kv_full[st], (int)(2 * a.F + h * D + kd * 64), r);
-        }
-        issued[st] = true;
-        issued_phase[st] = ph;
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::kTile);
+      for (int t = 0; t < 2; ++t)
+        for (int kd = 0; kd < KD; ++kd)
+          tma_load_2d(sQ + t * Cfg::kTile + kd * (BQ * 128), &tm_qkv, q_full, (int)(h * D + kd * 64),
+                      row0 + m0 + t * BQ);
+      const int loads = 2 * nB;  // K_0, V_0, K_1, V_1, ...
+      int issued = 0;
+      for (int i = 0; i < loads; ++i) {
+        const int slot = i % NS;
+        const uint32_t use = (uint32_t)(i / NS);
+        if (!mbar_wait_bounded(&slot_empty[slot], (use & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 200)) break;
+        uint8_t* dst = sRing + slot * Cfg::kTile;
+        mbar_arrive_expect_tx(&slot_full[slot], Cfg::kTile);
+        const int col = (int)((i & 1) ? 2 * a.F : a.F) + h * D;
+        const int row = row0 + (i >> 1) * BKV;
+        for (int kd = 0; kd < KD; ++kd)
+          tma_load_2d(dst + kd * (BKV * 128), &tm_qkv, &slot_full[slot], col + kd * 64, row);
+        issued = i + 1;
       }
+      // drain: every issued copy lands before the CTA exits
       mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 201);
-      for (int s = 0; s < 2; ++s)
-        if (issued[s]) mbar_wait_bounded(&kv_full[s], issued_phase[s], a.status, kErrWaitTimeoutFull, 202);
+      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
+        mbar_wait_bounded(&slot_full[i % NS], (uint32_t)(i / NS) & 1u, a.status, kErrWaitTimeoutFull, 202);
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = make_idesc(1, 0, 0, BQ, BKV);  // Q K-major, K K-major
       constexpr uint32_t idesc_o = make_idesc(1, 0, 1, BQ, D);    // P K-major, V MN-major
-      bool ok = mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 210);
-      const uint32_t q_base = smem_u32(sQ);
-      auto issue_pv = [&](int jj) -> bool {
-        const int st = jj & 1;
-        const int ob = jj & 1;
-        const uint32_t ph = (jj >> 1) & 1;
-        const int pb = jj % Cfg::kPBuffers;
-        if (!mbar_wait_bounded(&p_full[jj & 1], ph, a.status, kErrWaitTimeoutAccum, 211)) return false;
-        if (!mbar_wait_bounded(&o_free[ob], ph ^ 1u, a.status, kErrWaitTimeoutAccum, 212)) return false;
+      // descriptors with a zero start address; the start field (address >> 4)
+      // is added per operand and stays below 2^14 (shared memory < 256 KB)
+      const uint64_t kmaj = make_smem_desc(0, 16, 1024, kSwizzle128B);
+      const uint64_t mnmaj = make_smem_desc(0, BKV * 128, 1024, kSwizzle128B);
+      const uint32_t q16 = smem_u32(sQ) >> 4, ring16 = smem_u32(sRing) >> 4, p16 = smem_u32(sP) >> 4;
+      auto slot_of = [&](int i) { return (uint32_t)(i % NS); };
+      auto phase_of = [&](int i) { return (uint32_t)(i / NS) & 1u; };
+      auto issue_s = [&](int t, int j) -> bool {
+        if (j > 0 && !mbar_wait_bounded(&s_free[t], (uint32_t)(j - 1) & 1u, a.status, kErrWaitTimeoutAccum, 211))
+          return false;
         tc_fence_after();
-        const uint32_t p_base = smem_u32(sP + pb * Cfg::kPBytes);
-        const uint32_t v_base = smem_u32(sKV + st * Cfg::kStageBytes + Cfg::kKBytes);
+        const uint64_t ad = kmaj + q16 + t * (Cfg::kTile >> 4);
+        const uint64_t bd = kmaj + ring16 + slot_of(2 * j) * (Cfg::kTile >> 4);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t ad = make_smem_desc(p_base + (kk >> 2) * (BQ * 128) + (kk & 3) * 32, 16, 1024, kSwizzle128B);
-          const uint64_t bd = make_smem_desc(v_base + kk * 16 * 128, BKV * 128, 1024, kSwizzle128B);
-          tc_mma_f16(tmem + Cfg::kOCol + ob * D, ad, bd, idesc_o, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
+          tc_mma_f16(tmem + Cfg::kSCol + t * BKV, ad + off, bd + off, idesc_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&o_full[ob]);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&s_full[t]);
         return true;
       };
-      for (int j = 0; j < nblocks && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(&kv_full[st], ph, a.status, kErrWaitTimeoutFull, 213) ||
-            !mbar_wait_bounded(&s_free[st], ph ^ 1u, a.status, kErrWaitTimeoutAccum, 214)) {
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait_bounded(&p_full[t], (uint32_t)j & 1u, a.status, kErrWaitTimeoutAccum, 212) ||
+            !mbar_wait_bounded(&slot_full[slot_of(2 * j + 1)], phase_of(2 * j + 1), a.status, kErrWaitTimeoutFull,
+                               213))
+          return false;
+        tc_fence_after();
+        const uint64_t ad = kmaj + p16 + t * (Cfg::kPBytes >> 4);
+        const uint64_t bd = mnmaj + ring16 + slot_of(2 * j + 1) * (Cfg::kTile >> 4);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint32_t aoff = ((kk >> 2) * (BQ * 128) + (kk & 3) * 32) >> 4;
+          tc_mma_f16(tmem + Cfg::kOCol + t * D, ad + aoff, bd + ((kk * 16 * 128) >> 4), idesc_o,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&o_done[t]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 210);
+      for (int j = 0; j < nB && ok; ++j) {
+        if (!mbar_wait_bounded(&slot_full[slot_of(2 * j)], phase_of(2 * j), a.status, kErrWaitTimeoutFull, 214)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sKV + st * Cfg::kStageBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t sub = (kk >> 2) * (BQ * 128), off = (kk & 3) * 32;
-          const uint64_t ad = make_smem_desc(q_base + sub + off, 16, 1024, kSwizzle128B);
-          const uint64_t bd = make_smem_desc(k_base + (kk >> 2) * (BKV * 128) + off, 16, 1024, kSwizzle128B);
-          tc_mma_f16(tmem + Cfg::kSCol + st * BKV, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        if (j < nA && !issue_s(0, j)) {
+          ok = false;
+          break;
         }
-        tc_commit(&s_full[st]);
-        if (j >= 1 && !issue_pv(j - 1)) {
+        if (j >= 1) {
+          if (!issue_pv(1, j - 1)) {
+            ok = false;
+            break;
+          }
+          tc_commit(&slot_empty[slot_of(2 * (j - 1) + 1)]);  // V_{j-1} read by both tiles
+        }
+        if (!issue_s(1, j)) {
+          ok = false;
+          break;
+        }
+        tc_commit(&slot_empty[slot_of(2 * j)]);  // K_j read by both tiles
+        if (j < nA && !issue_pv(0, j)) {
           ok = false;
           break;
         }
       }
-      if (ok && nblocks > 0) issue_pv(nblocks - 1);
+      if (ok && nB > 0 && issue_pv(1, nB - 1)) tc_commit(&slot_empty[slot_of(2 * (nB - 1) + 1)]);
       tc_commit(done);
       mbar_wait_bounded(done, 0, a.status, kErrWaitTimeoutAccum, 215);
     }
-  } else {
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;             // tile 0 (A) or 1 (B)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;   // query row within the tile == TMEM lane
-    const int q = m0 + r;
+    const int q = m0 + t * BQ + r;
+    const int nblk = t ? nB : nA;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    float o_acc[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o_acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, alpha_pending = 1.f;
+    const uint32_t s_col = lane_base + Cfg::kSCol + t * BKV;
+    const uint32_t o_col = lane_base + Cfg::kOCol + t * D;
+    uint8_t* prow = sP + t * Cfg::kPBytes + r * 128;
+    const int key_limit = a.causal ? min(q + 1, T) : T;  // keys [0, key_limit) are visible
+    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    auto fold_o = [&](int jj, float alpha) -> bool {
-      const int ob = jj & 1;
-      const uint32_t ph = (jj >> 1) & 1;
-      if (!mbar_wait_warp(&o_full[ob], ph, a.status, kErrWaitTimeoutAccum, 220)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tld32(lane_base + Cfg::kOCol + ob * D + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha + v[i];
-      }
-      tc_fence_before();
-      mbar_arrive(&o_free[ob]);
-      return true;
-    };
-    for (int j = 0; j < nblocks && ok; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      const int n0 = j * BKV;
-      if (!mbar_wait_warp(&s_full[st], ph, a.status, kErrWaitTimeoutAccum, 221)) {
+    for (int j = 0; j < nblk && ok; ++j) {
+      if (!mbar_wait_warp(&s_full[t], (uint32_t)j & 1u, a.status, kErrWaitTimeoutAccum, 220)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool need_mask = (a.causal && n0 + BKV - 1 > m0) || (n0 + BKV > T);
-      const uint32_t s_base = lane_base + Cfg::kSCol + st * BKV;
-      // pass 1: row max
-      float mx = -INFINITY;
+      uint32_t sr[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        float v[32];
-        tld32(s_base + c * 32, v);
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld_32x32b_x32_async(s_col + c * 32, sr + c * 32);
+      tmem_wait_ld_regs<BKV>(sr);
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);  // S_t may be overwritten by the next block
+      const int lim = key_limit - j * BKV;  // visible columns of this block: [0, lim)
+      if (lim < BKV) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = v[i] * a.sl2;
-          const int key = n0 + c * 32 + i;
-          if (need_mask && (key >= T || (a.causal && key > q))) x = -INFINITY;
-          mx = fmaxf(mx, x);
-        }
+        for (int i = 0; i < BKV; ++i)
+          if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m_run, mx);
+      float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+#pragma unroll
+      for (int i = 2; i < BKV; i += 2) {
+        mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
+        mx1 = fmaxf(mx1, __uint_as_float(sr[i + 1]));
+      }
+      const float mx = fmaxf(mx0, mx1);
+      const float m_blk = mx * a.sl2;
+      const bool rescale = m_blk > m_run + kRescaleThreshold;
+      const float m_new = rescale ? m_blk : m_run;
+      const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.f;  // 0 while m_run = -inf
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2f(m_run - base);
-      // the P buffer of block j is free once the PV MMA of block j - kPBuffers retired
-      if (j >= Cfg::kPBuffers) {
-        const int prev = j - Cfg::kPBuffers;
-        if (!mbar_wait_warp(&o_full[prev & 1], (prev >> 1) & 1, a.status, kErrWaitTimeoutAccum, 222)) {
+      float rs = 0.f;
+      uint32_t pk[BKV / 2];
+#pragma unroll
+      for (int i = 0; i < BKV / 2; ++i) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), a.sl2, -base));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), a.sl2, -base));
+        rs += p0 + p1;
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      // PV(j-1) finished: the P tile is free and O_t holds blocks < j
+      if (j > 0) {
+        if (!mbar_wait_warp(&o_done[t], (uint32_t)(j - 1) & 1u, a.status, kErrWaitTimeoutAccum, 221)) {
           ok = false;
           break;
         }
-      }
-      // pass 2: p = exp2(s - m), row sum, bf16 P row into the swizzled A tile
-      uint8_t* prow = sP + (j % Cfg::kPBuffers) * Cfg::kPBytes;
-      float rs = 0.f;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32_async(o_col + c * 32, ov);
+            tmem_wait_ld_regs<32>(ov);
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        float v[32];
-        tld32(s_base + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = v[i] * a.sl2;
-          const int key = n0 + c * 32 + i;
-          if (need_mask && (key >= T || (a.causal && key > q))) x = -INFINITY;
-          v[i] = exp2f(x - base);
-          rs += v[i];
-        }
-        // 32 keys = 4 chunks of 8 -> 16-byte stores at swizzled positions
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int chunk = c * 4 + g;          // 0..15 over the 128 keys
-          const int sub = chunk >> 3, ch = chunk & 7;
-          __align__(16) __nv_bfloat162 hv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) hv[e] = __floats2bfloat162_rn(v[g * 8 + 2 * e], v[g * 8 + 2 * e + 1]);
-          uint8_t* dst = prow + sub * (BQ * 128) + r * 128 + ((ch ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<uint4*>(hv);
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st_32x32b_x32(o_col + c * 32, ov);
+          }
+          tmem_wait_st();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[st]);  // S[st] fully read
-      fence_proxy_async_smem();  // make the P stores visible to the tensor core
-      mbar_arrive(&p_full[st]);
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      if (j >= 1 && !fold_o(j - 1, alpha_pending)) {
-        ok = false;
-        break;
+      // P row -> swizzled A tile: 16 chunks of 8 keys, chunk ch of sub-tile ch / 8
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const int sub = ch >> 3, c8 = ch & 7;
+        const uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + sub * (BQ * 128) + ((c8 ^ (r & 7)) << 4)) = v;
       }
-      alpha_pending = alpha;
+      fence_proxy_async_smem();  // P stores visible to the tensor core
+      tc_fence_before();         // O rescale stores ordered before the next MMA
+      mbar_arrive(&p_full[t]);
     }
-    if (ok && nblocks > 0) ok = fold_o(nblocks - 1, alpha_pending);
-    // epilogue: O / l and LSE
-    if (ok && q < T) {
+    if (ok && nblk > 0)
+      ok = mbar_wait_warp(&o_done[t], (uint32_t)(nblk - 1) & 1u, a.status, kErrWaitTimeoutAccum, 222);
+    // epilogue: O / l and LSE (TMEM loads in every lane, stores for rows < T)
+    if (ok) {
+      tc_fence_after();
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
       __nv_bfloat16* orow = a.o + (long long)(b * T + q) * a.o_stride_t + h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32_async(o_col + c * 32, ov);
+        tmem_wait_ld_regs<32>(ov);
+        if (q < T) {
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        __align__(16) __nv_bfloat162 hv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) hv[e] = __floats2bfloat162_rn(o_acc[c * 8 + 2 * e] * inv, o_acc[c * 8 + 2 * e + 1] * inv);
-        *reinterpret_cast<uint4*>(orow + c * 8) = *reinterpret_cast<uint4*>(hv);
+          for (int g = 0; g < 4; ++g) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(ov[g * 8 + 0]) * inv, __uint_as_float(ov[g * 8 + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(ov[g * 8 + 2]) * inv, __uint_as_float(ov[g * 8 + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(ov[g * 8 + 4]) * inv, __uint_as_float(ov[g * 8 + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(ov[g * 8 + 6]) * inv, __uint_as_float(ov[g * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
+          }
+        }
       }
-      a.lse[(long long)bh * T + q] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
+      if (q < T) a.lse[(long long)bh * T + q] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
@@ -337,21 +371,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int D>
 void launch_fwd(const AttnParams& p, cudaStream_t s) {
-  using Cfg = FaCfg<D>;
+  using Cfg = FwdCfg<D>;
   static bool attr = false;
   if (!attr) {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
+    // setmaxnreg redistributes exactly the launch allocation; any other
+    // launch count would make the increase wait for registers that never come
+    cudaFuncAttributes fa{};
+    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D>));
+    if (fa.numRegs != kLaunchRegs)
+      throw std::runtime_error("fa_fwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
+                               " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
     attr = true;
   }
   const long long F = (long long)p.H * D;
   // q, k, v are column blocks of one [B*T, 3F] matrix (the fused projection)
-  const long long row_stride = p.q_stride_t;
-  CUtensorMap tm = make_tmap_bf16_2d(p.q, (uint64_t)(3 * F), (uint64_t)p.B * p.T, (uint64_t)row_stride, 64, 128);
-  FaTcArgs a{};
-  a.B = p.B;
+  CUtensorMap tm = make_tmap_bf16_2d(p.q, (uint64_t)(3 * F), (uint64_t)p.B * p.T, (uint64_t)p.q_stride_t, 64, 128);
+  FwdArgs a{};
   a.H = p.H;
   a.T = p.T;
-  a.D = D;
   a.F = F;
   a.sl2 = p.scale * kLog2e;
   a.causal = p.causal;
@@ -359,7 +397,7 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
   a.o_stride_t = p.o_stride_t;
   a.lse = p.lse;
   a.status = device_status_ptr();
-  dim3 grid((p.T + BQ - 1) / BQ, p.B * p.H);
+  dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
   fa_fwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
@@ -373,7 +411,7 @@ bool flash_attn_fwd_tc_supported(const AttnParams& p) {
   return (p.D == 64 || p.D == 128) && p.k == p.q + F && p.v == p.q + 2 * F && p.q_stride_t == 3 * F &&
          p.k_stride_t == 3 * F && p.v_stride_t == 3 * F && p.q_stride_b == (long long)p.T * 3 * F &&
          p.o_stride_b == (long long)p.T * p.o_stride_t && (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0 &&
-         (p.o_stride_t % 8) == 0;
+         (reinterpret_cast<uintptr_t>(p.o) & 15u) == 0 && (p.o_stride_t % 8) == 0;
 }
 
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s) {

@@ -3,31 +3,40 @@
 // One CTA owns a block of 128 keys of one (batch, head) and loops over the
 // 128-query blocks that attend to it (causal: from the diagonal on).
 //
-//   warp 0      TMA producer: K, V once; Q_i, dO_i per query block (ring),
-//               plus lse_i / delta_i into shared memory
-//   warp 1      TMEM allocator + MMA issuer (one elected thread), per block i:
-//                 S^T  = K Q_i^T           M=128 keys, N=128 queries, K=D
-//                 dP^T = V dO_i^T          (same shape)
-//                 dV  += P^T dO_i          M=128 keys, N=D, K=128 queries
-//                 dK  += dS^T Q_i          (same)
-//                 dQ_i = dS K              M=128 queries, N=D, K=128 keys
-//               (dS is read MN-major from the dS^T tile; dO_i, Q_i and K are
-//               read MN-major as the B operands of the last three products)
-//   warps 2..9  two warpgroups; TMEM lane r (warp%4 picks the lane quarter)
-//               is key row r and warpgroup g takes query columns
-//               [64g, 64g+64): P^T = exp2(S^T*scale*log2e - lse),
+//   warps 0..7  two compute warpgroups; TMEM lane r (warp%4 picks the lane
+//               quarter) is key row r and warpgroup g takes query columns
+//               [64g, 64g+64).  Each thread loads its 64 S^T and 64 dP^T
+//               values with four TMEM loads and one wait, frees S^T / dP^T,
+//               and computes P^T = exp2(S^T*scale*log2e - lse) and
 //               dS^T = P^T (dP^T - delta), both written as bf16 into the
 //               swizzled shared tiles (warpgroup g fills sub-tile g); then
 //               lane r takes query row r, columns [gD/2, gD/2+D/2) of dQ_i
 //               from TMEM and adds them into the fp32 dQ accumulator in
 //               global memory (vector reductions); at the end the same split
 //               stores dK (scaled) and dV.
+//   warp 8      TMA producer: K, V once; Q_i, dO_i per query block (ring),
+//               plus lse_i / delta_i into shared memory
+//   warp 9      TMEM allocator + MMA issuer (one elected thread), per block i:
+//                 S^T  = K Q_i^T           M=128 keys, N=128 queries, K=D
+//                 dP^T = V dO_i^T          (same shape)
+//                 dV  += P^T dO_i          M=128 keys, N=D, K=128 queries
+//                 dK  += dS^T Q_i          (same)
+//                 dQ_i = dS K              M=128 queries, N=D, K=128 keys
+//               (dS is read MN-major from the dS^T tile; dO_i, Q_i and K are
+//               read MN-major as the B operands of the last three products).
+//               For D = 64, S^T / dP^T of block i+1 are issued as soon as the
+//               compute warps hold block i in registers, so they overlap the
+//               softmax of block i.
 //
 // TMEM: S^T [0,128), dP^T [128,256), dV, dK, dQ after that (dQ reuses the
-// S^T columns when D = 128).  Every wait is bounded.
+// S^T columns when D = 128, which keeps that case in step order).
+// Registers: 384 threads launch with 168 each; warpgroup 2 gives back down to
+// 80 and the compute warpgroups take 208 (the host checks the launch count).
+// Every wait is bounded.
 #include <cudaTypedefs.h>
 
 #include <stdexcept>
+#include <string>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -41,8 +50,12 @@ namespace {
 
 constexpr int BK = 128;  // keys per CTA
 constexpr int BQ = 128;  // queries per step
-constexpr int kCompute = 256;  // warps 2..9
-constexpr int kThreads = 64 + kCompute;
+constexpr int kCompute = 256;      // warps 0..7
+constexpr int kThreads = 384;      // 3 warpgroups
+constexpr int kLaunchRegs = 168;   // 65536 / 384, rounded down to 8
+constexpr int kComputeRegs = 208;
+constexpr int kServiceRegs = 80;
+static_assert(2 * 128 * kComputeRegs + 128 * kServiceRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -78,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int KD = D / 64;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint8_t* sK = smem;
   uint8_t* sV = sK + Cfg::kTile;
   uint8_t* sQD = sV + Cfg::kTile;                 // [S][Q | dO]
@@ -90,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qd_full = bars + 1;      // [2]
   uint64_t* qd_empty = bars + 3;     // [2]
   uint64_t* s_full = bars + 5;       // S^T and dP^T ready
-  uint64_t* s_free = bars + 6;       // S^T / dP^T read by all 128 threads
+  uint64_t* s_free = bars + 6;       // S^T / dP^T held in registers by all compute threads
   uint64_t* p_full = bars + 7;       // P^T / dS^T written
   uint64_t* dq_full = bars + 8;      // dQ_i ready (all MMAs of step i done)
   uint64_t* dq_free = bars + 9;      // dQ_i read
@@ -107,8 +120,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int i_end = (T + BQ - 1) / BQ;
   const int steps = i_end - i_start;
   const int row0 = b * T;
+  constexpr int kProducerWarp = 8, kMmaWarp = 9;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
     mbar_init(kv_full, 1);
@@ -125,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     fence_proxy_async_smem();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, Cfg::kCols);
     tmem_relinquish();
   }
@@ -134,7 +148,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= 8) {
+    // register counts are set at the top of each role's branch so the
+    // compiler allocates every region with the count it runs under
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kServiceRegs));
+  }
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     bool issued[2] = {false, false};
     uint32_t iph[2] = {0, 0};
@@ -145,17 +164,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sV + kd * (BK * 128), &tm_qkv, kv_full, (int)(2 * a.F + h * D + kd * 64), row0 + n0);
       }
     }
-    bool ok = true;
-    for (int t = 0; t < steps && ok; ++t) {
+    for (int t = 0; t < steps; ++t) {
       const int st = t % S;
       const uint32_t ph = (t / S) & 1;
       int good = 1;
       if (lane == 0) good = mbar_wait_bounded(&qd_empty[st], ph ^ 1u, a.status, kErrWaitTimeoutEmpty, 300);
       good = __shfl_sync(0xffffffffu, good, 0);
-      if (!good) {
-        ok = false;
-        break;
-      }
+      if (!good) break;
       const int q0 = (i_start + t) * BQ;
       // lse / delta of this query block (generic stores, ordered by the barrier arrive)
       float* vec = sVec + st * (2 * BQ);
@@ -182,84 +197,107 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s2 = 0; s2 < S; ++s2)
         if (issued[s2]) mbar_wait_bounded(&qd_full[s2], iph[s2], a.status, kErrWaitTimeoutFull, 302);
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t id_s = make_idesc(1, 0, 0, BK, BQ);   // K / V K-major, Q / dO K-major
       constexpr uint32_t id_kv = make_idesc(1, 0, 1, BK, D);   // P^T / dS^T K-major, dO / Q MN-major
       constexpr uint32_t id_q = make_idesc(1, 1, 1, BQ, D);    // dS MN-major, K MN-major
-      bool ok = mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 310);
-      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
-      const uint32_t pt_base = smem_u32(sPT), dst_base = smem_u32(sDST);
-      for (int t = 0; t < steps && ok; ++t) {
+      // descriptors with a zero start address; the start field (address >> 4)
+      // is added per operand and stays below 2^14 (shared memory < 256 KB)
+      const uint64_t kmaj = make_smem_desc(0, 16, 1024, kSwizzle128B);
+      const uint64_t mnmaj = make_smem_desc(0, 128 * 128, 1024, kSwizzle128B);  // 128-row operand tiles
+      const uint32_t k16 = smem_u32(sK) >> 4, v16 = smem_u32(sV) >> 4, qd16 = smem_u32(sQD) >> 4;
+      const uint32_t pt16 = smem_u32(sPT) >> 4, dst16 = smem_u32(sDST) >> 4;
+      auto issue_s = [&](int t) -> bool {
         const int st = t % S;
-        const uint32_t ph = (t / S) & 1;
-        const uint32_t tp = t & 1;
-        if (!mbar_wait_bounded(&qd_full[st], ph, a.status, kErrWaitTimeoutFull, 311) ||
-            !mbar_wait_bounded(s_free, tp ^ 1u, a.status, kErrWaitTimeoutAccum, 312)) {
-          ok = false;
-          break;
-        }
-        if (D == 128 && t > 0 && !mbar_wait_bounded(dq_free, (t - 1) & 1, a.status, kErrWaitTimeoutAccum, 313)) {
-          ok = false;  // dQ shares the S^T columns when D = 128
-          break;
-        }
+        if (!mbar_wait_bounded(&qd_full[st], (uint32_t)(t / S) & 1u, a.status, kErrWaitTimeoutFull, 311)) return false;
         tc_fence_after();
-        const uint32_t q_base = smem_u32(sQD + st * Cfg::kStageBytes);
-        const uint32_t do_base = q_base + Cfg::kTile;
-#pragma unroll
+        const uint32_t q16 = qd16 + st * (Cfg::kStageBytes >> 4), do16 = q16 + (Cfg::kTile >> 4);
+#pragma unroll 1
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem + Cfg::kST, make_smem_desc(k_base + off, 16, 1024, kSwizzle128B),
-                     make_smem_desc(q_base + off, 16, 1024, kSwizzle128B), id_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
+          tc_mma_f16(tmem + Cfg::kST, kmaj + k16 + off, kmaj + q16 + off, id_s, kk > 0 ? 1u : 0u);
         }
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem + Cfg::kDPT, make_smem_desc(v_base + off, 16, 1024, kSwizzle128B),
-                     make_smem_desc(do_base + off, 16, 1024, kSwizzle128B), id_s, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
+          tc_mma_f16(tmem + Cfg::kDPT, kmaj + v16 + off, kmaj + do16 + off, id_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(s_full);
-        if (!mbar_wait_bounded(p_full, tp, a.status, kErrWaitTimeoutAccum, 314)) {
-          ok = false;
-          break;
-        }
-        if (D == 64 && t > 0 && !mbar_wait_bounded(dq_free, (t - 1) & 1, a.status, kErrWaitTimeoutAccum, 315)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        return true;
+      };
+      auto issue_grads = [&](int t) {
+        const int st = t % S;
+        const uint32_t q16 = qd16 + st * (Cfg::kStageBytes >> 4), do16 = q16 + (Cfg::kTile >> 4);
         // dV += P^T dO ; dK += dS^T Q    (K = 128 queries: sub-tile kk>>2 of the P^T / dS^T tiles)
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-          const uint64_t bdo = make_smem_desc(do_base + kk * 16 * 128, BQ * 128, 1024, kSwizzle128B);
-          const uint64_t bq = make_smem_desc(q_base + kk * 16 * 128, BQ * 128, 1024, kSwizzle128B);
+          const uint32_t aoff = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
+          const uint32_t boff = (kk * 16 * 128) >> 4;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc_mma_f16(tmem + Cfg::kDV, make_smem_desc(pt_base + aoff, 16, 1024, kSwizzle128B), bdo, id_kv, acc);
-          tc_mma_f16(tmem + Cfg::kDK, make_smem_desc(dst_base + aoff, 16, 1024, kSwizzle128B), bq, id_kv, acc);
+          tc_mma_f16(tmem + Cfg::kDV, kmaj + pt16 + aoff, mnmaj + do16 + boff, id_kv, acc);
+          tc_mma_f16(tmem + Cfg::kDK, kmaj + dst16 + aoff, mnmaj + q16 + boff, id_kv, acc);
         }
         // dQ_i = dS K  (A = dS^T read MN-major: 64-query chunks are the two sub-tiles)
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t ad = make_smem_desc(dst_base + kk * 16 * 128, BK * 128, 1024, kSwizzle128B);
-          const uint64_t bd = make_smem_desc(k_base + kk * 16 * 128, BK * 128, 1024, kSwizzle128B);
-          tc_mma_f16(tmem + Cfg::kDQ, ad, bd, id_q, kk > 0 ? 1u : 0u);
+          const uint32_t off = (kk * 16 * 128) >> 4;
+          tc_mma_f16(tmem + Cfg::kDQ, mnmaj + dst16 + off, mnmaj + k16 + off, id_q, kk > 0 ? 1u : 0u);
         }
         tc_commit(dq_full);
         tc_commit(&qd_empty[st]);
+      };
+      bool ok = mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 310);
+      if (D == 64) {
+        // S^T / dP^T of block t+1 are issued before the gradients of block t
+        ok = ok && issue_s(0);
+        for (int t = 0; t < steps && ok; ++t) {
+          if (t + 1 < steps) {
+            if (!mbar_wait_bounded(s_free, (uint32_t)t & 1u, a.status, kErrWaitTimeoutAccum, 312) ||
+                !issue_s(t + 1)) {
+              ok = false;
+              break;
+            }
+          }
+          if (!mbar_wait_bounded(p_full, (uint32_t)t & 1u, a.status, kErrWaitTimeoutAccum, 314) ||
+              (t > 0 && !mbar_wait_bounded(dq_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 315))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_grads(t);
+        }
+      } else {
+        // dQ shares the S^T columns: strictly one block after the other
+        for (int t = 0; t < steps && ok; ++t) {
+          if (t > 0 && (!mbar_wait_bounded(s_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 312) ||
+                        !mbar_wait_bounded(dq_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 313))) {
+            ok = false;
+            break;
+          }
+          if (!issue_s(t) || !mbar_wait_bounded(p_full, (uint32_t)t & 1u, a.status, kErrWaitTimeoutAccum, 314)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_grads(t);
+        }
       }
       tc_commit(done);
       mbar_wait_bounded(done, 0, a.status, kErrWaitTimeoutAccum, 316);
     }
-  } else {
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kComputeRegs));
     // ------------------------------------------------------------ compute
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;   // warpgroup 0 or 1
+    const int half = warp >> 2;         // warpgroup 0 or 1
     const int r = quarter * 32 + lane;  // key row (S^T, dP^T, dV, dK) and query row (dQ)
     const int key = n0 + r;
     const bool kvalid = key < T;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* pt_row = sPT + half * (128 * 128) + r * 128;
+    uint8_t* dst_row = sDST + half * (128 * 128) + r * 128;
     bool ok = true;
     for (int t = 0; t < steps && ok; ++t) {
       const int st = t % S;
@@ -272,39 +310,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const float* lse = sVec + st * (2 * BQ);
-      const float* dlt = lse + BQ;
-      const bool diag = a.causal && (q0 < n0 + BK);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;  // 32-query chunk 0..3
-        float sv[32], pv[32];
-        tmem_ld_32x32b_x32(lb + Cfg::kST + c * 32, sv);
-        tmem_ld_32x32b_x32(lb + Cfg::kDPT + c * 32, pv);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qi = c * 32 + i;
-          float p = exp2f(sv[i] * a.sl2 - lse[qi]);
-          if (!kvalid || (diag && key > q0 + qi)) p = 0.f;
-          sv[i] = p;
-          pv[i] = p * (pv[i] - dlt[qi]);
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int ch = cc * 4 + g;  // 8-query chunk within sub-tile `half`
-          const uint32_t off = half * (128 * 128) + r * 128 + ((ch ^ (r & 7)) << 4);
-          __align__(16) __nv_bfloat162 hp[4], hd[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hp[e] = __floats2bfloat162_rn(sv[g * 8 + 2 * e], sv[g * 8 + 2 * e + 1]);
-            hd[e] = __floats2bfloat162_rn(pv[g * 8 + 2 * e], pv[g * 8 + 2 * e + 1]);
-          }
-          *reinterpret_cast<uint4*>(sPT + off) = *reinterpret_cast<uint4*>(hp);
-          *reinterpret_cast<uint4*>(sDST + off) = *reinterpret_cast<uint4*>(hd);
-        }
-      }
+      uint32_t sv[64], pv[64];
+      tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64, sv);
+      tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64 + 32, sv + 32);
+      tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64, pv);
+      tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64 + 32, pv + 32);
+      tmem_wait_ld_regs<64>(sv);
+      tmem_wait_ld_regs<64>(pv);
       tc_fence_before();
-      mbar_arrive(s_free);
+      mbar_arrive(s_free);  // S^T / dP^T may be overwritten
+      const float4* lse4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + half * 64);
+      const float4* dlt4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + BQ + half * 64);
+      // causal diagonal block: query column qi is visible for this key when qi >= key - q0
+      const int qmin = (!kvalid) ? BQ + 1 : ((a.causal && q0 < n0 + BK) ? key - q0 - half * 64 : 0);
+      uint32_t hp[32], hd[32];
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {
+        const float4 l = lse4[g], d = dlt4[g];
+        const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
+        float p[4], ds[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = g * 4 + e;
+          float x = ex2_approx(fmaf(__uint_as_float(sv[i]), a.sl2, -lv[e]));
+          if (i < qmin) x = 0.f;
+          p[e] = x;
+          ds[e] = x * (__uint_as_float(pv[i]) - dv[e]);
+        }
+        hp[g * 2] = pack_bf16x2(p[0], p[1]);
+        hp[g * 2 + 1] = pack_bf16x2(p[2], p[3]);
+        hd[g * 2] = pack_bf16x2(ds[0], ds[1]);
+        hd[g * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+      }
+      // P^T / dS^T tiles are free: the gradient MMAs of block t-1 finished
+      // (dq_full of t-1 was awaited before the dQ read-out below)
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const uint32_t off = (uint32_t)((ch ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(pt_row + off) = make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(dst_row + off) = make_uint4(hd[ch * 4], hd[ch * 4 + 1], hd[ch * 4 + 2], hd[ch * 4 + 3]);
+      }
       fence_proxy_async_smem();
       mbar_arrive(p_full);
       // dQ_i (query row r, this warpgroup's half of the columns) -> fp32 accumulator
@@ -317,13 +362,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dst = a.dq_accum + (((long long)b * T + qrow) * a.H + h) * D + half * (D / 2);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(lb + Cfg::kDQ + half * (D / 2) + c * 32, v);
+        uint32_t v[32];
+        tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + half * (D / 2) + c * 32, v);
+        tmem_wait_ld_regs<32>(v);
         if (qrow < T) {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
             atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e * 4),
-                      make_float4(v[e * 4], v[e * 4 + 1], v[e * 4 + 2], v[e * 4 + 3]));
+                      make_float4(__uint_as_float(v[e * 4]), __uint_as_float(v[e * 4 + 1]),
+                                  __uint_as_float(v[e * 4 + 2]), __uint_as_float(v[e * 4 + 3])));
         }
       }
       tc_fence_before();
@@ -337,20 +384,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat16* dv = dk + a.F;
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        float kv[32], vv[32];
-        tmem_ld_32x32b_x32(lb + Cfg::kDK + half * (D / 2) + c * 32, kv);
-        tmem_ld_32x32b_x32(lb + Cfg::kDV + half * (D / 2) + c * 32, vv);
+        uint32_t kv[32], vv[32];
+        tmem_ld_32x32b_x32_async(lb + Cfg::kDK + half * (D / 2) + c * 32, kv);
+        tmem_ld_32x32b_x32_async(lb + Cfg::kDV + half * (D / 2) + c * 32, vv);
+        tmem_wait_ld_regs<32>(kv);
+        tmem_wait_ld_regs<32>(vv);
         if (!kvalid) continue;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          __align__(16) __nv_bfloat162 hk[4], hv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hk[e] = __floats2bfloat162_rn(kv[g * 8 + 2 * e] * a.scale, kv[g * 8 + 2 * e + 1] * a.scale);
-            hv[e] = __floats2bfloat162_rn(vv[g * 8 + 2 * e], vv[g * 8 + 2 * e + 1]);
-          }
-          *reinterpret_cast<uint4*>(dk + c * 32 + g * 8) = *reinterpret_cast<uint4*>(hk);
-          *reinterpret_cast<uint4*>(dv + c * 32 + g * 8) = *reinterpret_cast<uint4*>(hv);
+          uint4 hk, hv;
+          hk.x = pack_bf16x2(__uint_as_float(kv[g * 8 + 0]) * a.scale, __uint_as_float(kv[g * 8 + 1]) * a.scale);
+          hk.y = pack_bf16x2(__uint_as_float(kv[g * 8 + 2]) * a.scale, __uint_as_float(kv[g * 8 + 3]) * a.scale);
+          hk.z = pack_bf16x2(__uint_as_float(kv[g * 8 + 4]) * a.scale, __uint_as_float(kv[g * 8 + 5]) * a.scale);
+          hk.w = pack_bf16x2(__uint_as_float(kv[g * 8 + 6]) * a.scale, __uint_as_float(kv[g * 8 + 7]) * a.scale);
+          hv.x = pack_bf16x2(__uint_as_float(vv[g * 8 + 0]), __uint_as_float(vv[g * 8 + 1]));
+          hv.y = pack_bf16x2(__uint_as_float(vv[g * 8 + 2]), __uint_as_float(vv[g * 8 + 3]));
+          hv.z = pack_bf16x2(__uint_as_float(vv[g * 8 + 4]), __uint_as_float(vv[g * 8 + 5]));
+          hv.w = pack_bf16x2(__uint_as_float(vv[g * 8 + 6]), __uint_as_float(vv[g * 8 + 7]));
+          *reinterpret_cast<uint4*>(dk + c * 32 + g * 8) = hk;
+          *reinterpret_cast<uint4*>(dv + c * 32 + g * 8) = hv;
         }
       }
     }
@@ -358,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kCols);
   }
@@ -370,6 +422,13 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
+    // setmaxnreg redistributes the launch allocation; a different launch count
+    // could make the increase wait for registers that never come
+    cudaFuncAttributes fa{};
+    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_bwd_tc_kernel<D>));
+    if (fa.numRegs != kLaunchRegs)
+      throw std::runtime_error("fa_bwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
+                               " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
     attr = true;
   }
   const long long F = (long long)p.f.H * D;
