@@ -279,28 +279,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < BKV; ++i)
           if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
       }
-      float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+      float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
 #pragma unroll
-      for (int i = 2; i < BKV; i += 2) {
-        mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
-        mx1 = fmaxf(mx1, __uint_as_float(sr[i + 1]));
+      for (int i = 4; i < BKV; i += 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx4[e] = fmaxf(mx4[e], __uint_as_float(sr[i + e]));
       }
-      const float mx = fmaxf(mx0, mx1);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_blk = mx * a.sl2;
       const bool rescale = m_blk > m_run + kRescaleThreshold;
       const float m_new = rescale ? m_blk : m_run;
       const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.f;  // 0 while m_run = -inf
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[BKV / 2];
 #pragma unroll
       for (int i = 0; i < BKV / 2; ++i) {
         const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), a.sl2, -base));
         const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), a.sl2, -base));
-        rs += p0 + p1;
+        rs4[(2 * i) & 3] += p0;
+        rs4[(2 * i + 1) & 3] += p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
-      l_run = l_run * alpha + rs;
+      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m_run = m_new;
       // PV(j-1) finished: the P tile is free and O_t holds blocks < j
       if (j > 0) {

@@ -45,6 +45,8 @@ namespace uhfs {
 
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                               uint32_t box_inner, uint32_t box_outer);
+CUtensorMap make_tmap_f32_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                             uint32_t box_inner, uint32_t box_outer);
 
 namespace {
 
@@ -65,7 +67,8 @@ struct BwdCfg {
   static constexpr int kStageBytes = 2 * kTile;      // Q_i | dO_i
   static constexpr int kPT = BK * BQ * 2;            // P^T or dS^T tile (2 sub-tiles of 128 x 64)
   static constexpr int kVec = 2 * BQ * 4;            // lse_i | delta_i
-  static constexpr int kSmem = 1024 + 2 * kTile + kStages * kStageBytes + 2 * kPT + kStages * kVec + 256;
+  static constexpr int kStage = 128 * 32 * 4;        // fp32 dQ staging box per warpgroup (128 rows x 32)
+  static constexpr int kSmem = 1024 + 2 * kTile + kStages * kStageBytes + 2 * kPT + kStages * kVec + 2 * kStage + 128;
   static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + D;
   static constexpr uint32_t kDQ = (D == 64) ? 256 + 2 * D : 0;  // D=128: reuse S^T columns
   static constexpr uint32_t kCols = 512;
@@ -86,7 +89,7 @@ struct BwdArgs {
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                     const BwdArgs a) {
+                     const __grid_constant__ CUtensorMap tm_dq, const BwdArgs a) {
   using Cfg = BwdCfg<D>;
   constexpr int KD = D / 64;
   constexpr int S = Cfg::kStages;
@@ -98,17 +101,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sPT = sQD + S * Cfg::kStageBytes;      // P^T
   uint8_t* sDST = sPT + Cfg::kPT;                 // dS^T
   float* sVec = reinterpret_cast<float*>(sDST + Cfg::kPT);  // [S][lse(128) | delta(128)]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sVec) + S * Cfg::kVec);
+  uint8_t* sStage = reinterpret_cast<uint8_t*>(sVec) + S * Cfg::kVec;  // [2 warpgroups] fp32 dQ boxes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 2 * Cfg::kStage);
   uint64_t* kv_full = bars;          // 1
   uint64_t* qd_full = bars + 1;      // [2]
   uint64_t* qd_empty = bars + 3;     // [2]
   uint64_t* s_full = bars + 5;       // S^T and dP^T ready
   uint64_t* s_free = bars + 6;       // S^T / dP^T held in registers by all compute threads
   uint64_t* p_full = bars + 7;       // P^T / dS^T written
-  uint64_t* dq_full = bars + 8;      // dQ_i ready (all MMAs of step i done)
+  uint64_t* dq_full = bars + 8;      // dQ_i ready (dQ MMAs of step i done)
   uint64_t* dq_free = bars + 9;      // dQ_i read
-  uint64_t* done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* pt_free = bars + 10;     // dV / dK MMAs of step i done: P^T / dS^T reusable
+  uint64_t* done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -125,9 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_full[i], 2);  // TMA bytes + the producer's lse / delta stores
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(s_full, 1);
@@ -135,6 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(p_full, kCompute);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, kCompute);
+    mbar_init(pt_free, 1);
     mbar_init(done, 1);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -172,14 +179,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       good = __shfl_sync(0xffffffffu, good, 0);
       if (!good) break;
       const int q0 = (i_start + t) * BQ;
-      // lse / delta of this query block (generic stores, ordered by the barrier arrive)
-      float* vec = sVec + st * (2 * BQ);
-      for (int x = lane; x < BQ; x += 32) {
-        const int qq = q0 + x;
-        vec[x] = qq < T ? a.lse[(long long)bh * T + qq] : INFINITY;
-        vec[BQ + x] = qq < T ? a.delta[(long long)bh * T + qq] : 0.f;
-      }
-      __syncwarp();
       if (lane == 0) {
         uint8_t* sQ = sQD + st * Cfg::kStageBytes;
         uint8_t* sDO = sQ + Cfg::kTile;
@@ -191,6 +190,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued[st] = true;
         iph[st] = ph;
       }
+      // lse / delta of this query block: all loads in flight at once, then the
+      // stores, ordered before the second arrival on qd_full
+      float lv[BQ / 32], dv[BQ / 32];
+#pragma unroll
+      for (int k = 0; k < BQ / 32; ++k) {
+        const int qq = q0 + k * 32 + lane;
+        lv[k] = qq < T ? __ldg(a.lse + (long long)bh * T + qq) : INFINITY;
+        dv[k] = qq < T ? __ldg(a.delta + (long long)bh * T + qq) : 0.f;
+      }
+      float* vec = sVec + st * (2 * BQ);
+#pragma unroll
+      for (int k = 0; k < BQ / 32; ++k) {
+        vec[k * 32 + lane] = lv[k];
+        vec[BQ + k * 32 + lane] = dv[k];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qd_full[st]);
     }
     if (lane == 0) {
       mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 301);
@@ -230,6 +246,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_grads = [&](int t) {
         const int st = t % S;
         const uint32_t q16 = qd16 + st * (Cfg::kStageBytes >> 4), do16 = q16 + (Cfg::kTile >> 4);
+        // dQ_i = dS K first (A = dS^T read MN-major: 64-query chunks are the
+        // two sub-tiles), so its read-out overlaps the dV / dK products
+#pragma unroll 1
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint32_t off = (kk * 16 * 128) >> 4;
+          tc_mma_f16(tmem + Cfg::kDQ, mnmaj + dst16 + off, mnmaj + k16 + off, id_q, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(dq_full);
         // dV += P^T dO ; dK += dS^T Q    (K = 128 queries: sub-tile kk>>2 of the P^T / dS^T tiles)
 #pragma unroll 1
         for (int kk = 0; kk < BQ / 16; ++kk) {
@@ -239,13 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16(tmem + Cfg::kDV, kmaj + pt16 + aoff, mnmaj + do16 + boff, id_kv, acc);
           tc_mma_f16(tmem + Cfg::kDK, kmaj + dst16 + aoff, mnmaj + q16 + boff, id_kv, acc);
         }
-        // dQ_i = dS K  (A = dS^T read MN-major: 64-query chunks are the two sub-tiles)
-#pragma unroll 1
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint32_t off = (kk * 16 * 128) >> 4;
-          tc_mma_f16(tmem + Cfg::kDQ, mnmaj + dst16 + off, mnmaj + k16 + off, id_q, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(dq_full);
+        tc_commit(pt_free);
         tc_commit(&qd_empty[st]);
       };
       bool ok = mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 310);
@@ -298,88 +316,111 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* pt_row = sPT + half * (128 * 128) + r * 128;
     uint8_t* dst_row = sDST + half * (128 * 128) + r * 128;
+    uint8_t* stage = sStage + half * Cfg::kStage;
+    const bool leader = quarter == 0 && lane == 0;  // issues this warpgroup's TMA reductions
+    // Failures are warp-uniform but not warpgroup-uniform, so every thread
+    // runs the same sequence of named barriers for every step; after a failed
+    // wait a thread only skips the work.
     bool ok = true;
-    for (int t = 0; t < steps && ok; ++t) {
+    for (int t = 0; t < steps; ++t) {
       const int st = t % S;
       const uint32_t tp = t & 1;
       const int q0 = (i_start + t) * BQ;
       // qd_full orders the producer's lse / delta stores before our reads
-      if (!mbar_wait_warp(&qd_full[st], (t / S) & 1, a.status, kErrWaitTimeoutFull, 320) ||
-          !mbar_wait_warp(s_full, tp, a.status, kErrWaitTimeoutAccum, 321)) {
+      if (ok && (!mbar_wait_warp(&qd_full[st], (t / S) & 1, a.status, kErrWaitTimeoutFull, 320) ||
+                 !mbar_wait_warp(s_full, tp, a.status, kErrWaitTimeoutAccum, 321)))
         ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sv[64], pv[64];
-      tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64, sv);
-      tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64 + 32, sv + 32);
-      tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64, pv);
-      tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64 + 32, pv + 32);
-      tmem_wait_ld_regs<64>(sv);
-      tmem_wait_ld_regs<64>(pv);
-      tc_fence_before();
-      mbar_arrive(s_free);  // S^T / dP^T may be overwritten
-      const float4* lse4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + half * 64);
-      const float4* dlt4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + BQ + half * 64);
-      // causal diagonal block: query column qi is visible for this key when qi >= key - q0
-      const int qmin = (!kvalid) ? BQ + 1 : ((a.causal && q0 < n0 + BK) ? key - q0 - half * 64 : 0);
-      uint32_t hp[32], hd[32];
+      if (ok) {
+        tc_fence_after();
+        uint32_t sv[64], pv[64];
+        tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64, sv);
+        tmem_ld_32x32b_x32_async(lb + Cfg::kST + half * 64 + 32, sv + 32);
+        tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64, pv);
+        tmem_ld_32x32b_x32_async(lb + Cfg::kDPT + half * 64 + 32, pv + 32);
+        tmem_wait_ld_regs<64>(sv);
+        tmem_wait_ld_regs<64>(pv);
+        tc_fence_before();
+        mbar_arrive(s_free);  // S^T / dP^T may be overwritten
+        const float4* lse4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + half * 64);
+        const float4* dlt4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + BQ + half * 64);
+        // causal diagonal block: query column qi is visible for this key when qi >= key - q0
+        const int qmin = (!kvalid) ? BQ + 1 : ((a.causal && q0 < n0 + BK) ? key - q0 - half * 64 : 0);
+        uint32_t hp[32], hd[32];
 #pragma unroll
-      for (int g = 0; g < 16; ++g) {
-        const float4 l = lse4[g], d = dlt4[g];
-        const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
-        float p[4], ds[4];
+        for (int g = 0; g < 16; ++g) {
+          const float4 l = lse4[g], d = dlt4[g];
+          const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
+          float p[4], ds[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = g * 4 + e;
-          float x = ex2_approx(fmaf(__uint_as_float(sv[i]), a.sl2, -lv[e]));
-          if (i < qmin) x = 0.f;
-          p[e] = x;
-          ds[e] = x * (__uint_as_float(pv[i]) - dv[e]);
+          for (int e = 0; e < 4; ++e) {
+            const int i = g * 4 + e;
+            float x = ex2_approx(fmaf(__uint_as_float(sv[i]), a.sl2, -lv[e]));
+            if (i < qmin) x = 0.f;
+            p[e] = x;
+            ds[e] = x * (__uint_as_float(pv[i]) - dv[e]);
+          }
+          hp[g * 2] = pack_bf16x2(p[0], p[1]);
+          hp[g * 2 + 1] = pack_bf16x2(p[2], p[3]);
+          hd[g * 2] = pack_bf16x2(ds[0], ds[1]);
+          hd[g * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
         }
-        hp[g * 2] = pack_bf16x2(p[0], p[1]);
-        hp[g * 2 + 1] = pack_bf16x2(p[2], p[3]);
-        hd[g * 2] = pack_bf16x2(ds[0], ds[1]);
-        hd[g * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
-      }
-      // P^T / dS^T tiles are free: the gradient MMAs of block t-1 finished
-      // (dq_full of t-1 was awaited before the dQ read-out below)
+        // P^T / dS^T tiles are free once the gradient MMAs of block t-1 finished
+        if (t > 0 && !mbar_wait_warp(pt_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 323))
+          ok = false;
+        if (ok) {
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const uint32_t off = (uint32_t)((ch ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(pt_row + off) = make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(dst_row + off) = make_uint4(hd[ch * 4], hd[ch * 4 + 1], hd[ch * 4 + 2], hd[ch * 4 + 3]);
+          for (int ch = 0; ch < 8; ++ch) {
+            const uint32_t off = (uint32_t)((ch ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(pt_row + off) =
+                make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
+            *reinterpret_cast<uint4*>(dst_row + off) =
+                make_uint4(hd[ch * 4], hd[ch * 4 + 1], hd[ch * 4 + 2], hd[ch * 4 + 3]);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(p_full);
+          if (!mbar_wait_warp(dq_full, tp, a.status, kErrWaitTimeoutAccum, 322)) ok = false;
+        }
       }
-      fence_proxy_async_smem();
-      mbar_arrive(p_full);
-      // dQ_i (query row r, this warpgroup's half of the columns) -> fp32 accumulator
-      if (!mbar_wait_warp(dq_full, tp, a.status, kErrWaitTimeoutAccum, 322)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int qrow = q0 + r;
-      float* dst = a.dq_accum + (((long long)b * T + qrow) * a.H + h) * D + half * (D / 2);
-#pragma unroll
+      // dQ_i: TMEM -> registers -> swizzled fp32 box -> TMA reduce-add into
+      // the fp32 accumulator.  Rows past T add zeros (P is 0 there).
+#pragma unroll 1
       for (int c = 0; c < D / 64; ++c) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + half * (D / 2) + c * 32, v);
-        tmem_wait_ld_regs<32>(v);
-        if (qrow < T) {
+        if (ok) {
+          tc_fence_after();
+          tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + half * (D / 2) + c * 32, v);
+          tmem_wait_ld_regs<32>(v);
+          if (c == D / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(dq_free);  // TMEM dQ may be overwritten
+          }
+        }
+        if (leader) bulk_wait_group_read0();  // the previous reduction has read the box
+        named_barrier_sync(1 + half, 128);
+        if (ok) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e * 4),
-                      make_float4(__uint_as_float(v[e * 4]), __uint_as_float(v[e * 4 + 1]),
-                                  __uint_as_float(v[e * 4 + 2]), __uint_as_float(v[e * 4 + 3])));
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
+          fence_proxy_async_smem();
+        }
+        named_barrier_sync(1 + half, 128);
+        if (leader && ok) {
+          tma_reduce_add_2d(&tm_dq, stage, h * D + half * (D / 2) + c * 32, row0 + q0);
+          bulk_commit_group();
         }
       }
-      tc_fence_before();
-      mbar_arrive(dq_free);
     }
+    if (leader) bulk_wait_group0();
+    // the last dV / dK products have retired
+    if (ok && steps > 0 &&
+        !mbar_wait_warp(pt_free, (uint32_t)(steps - 1) & 1u, a.status, kErrWaitTimeoutAccum, 324))
+      ok = false;
     // dK (scaled) and dV: key row r, this warpgroup's half of the columns.
     // `ok` is warp-uniform (mbar_wait_warp); the TMEM loads are warp-collective
     // and run in every lane, only the stores depend on the key being in range.
     if (ok) {
+      tc_fence_after();
       __nv_bfloat16* dk = a.dqkv + (long long)(row0 + key) * 3 * a.F + a.F + h * D + half * (D / 2);
       __nv_bfloat16* dv = dk + a.F;
 #pragma unroll
@@ -434,6 +475,8 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   const long long F = (long long)p.f.H * D;
   CUtensorMap tq = make_tmap_bf16_2d(p.f.q, (uint64_t)(3 * F), (uint64_t)p.f.B * p.f.T, (uint64_t)(3 * F), 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(p.dout, (uint64_t)F, (uint64_t)p.f.B * p.f.T, (uint64_t)p.do_stride_t, 64, 128);
+  // dQ accumulator [B*T, H*D] fp32, reduced into in boxes of 32 columns x 128 rows
+  CUtensorMap tdq = make_tmap_f32_2d(p.dq_accum, (uint64_t)F, (uint64_t)p.f.B * p.f.T, (uint64_t)F, 32, 128);
   BwdArgs a{};
   a.B = p.f.B;
   a.H = p.f.H;
@@ -448,7 +491,7 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   a.dqkv = p.dq;
   a.status = device_status_ptr();
   dim3 grid((p.f.T + BK - 1) / BK, p.f.B * p.f.H);
-  fa_bwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tq, td, a);
+  fa_bwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tq, td, tdq, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

@@ -482,6 +482,22 @@ CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, 
   return m;
 }
 
+CUtensorMap make_tmap_f32_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                             uint32_t box_inner, uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  if ((row_stride_elems * 4) % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0) return;
   if (p.K <= 0) throw std::runtime_error("gemm: K must be positive");
