@@ -171,6 +171,15 @@ __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, const void* 
       : "memory");
 }
 
+// Shared tile -> global through the tensor map (TMA store); elements outside
+// the tensor are not written.  Same coordinate rules as the reduce above.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int coord0, int coord1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(smem_u32(smem_src)), "r"(coord0), "r"(coord1)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Wait until this thread's bulk operations have finished reading shared memory.
@@ -385,6 +394,34 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
   float t = tanhf(u);
   float du = k0 * (1.0f + 3.0f * k1 * x2);
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * du;
+}
+
+// Hardware tanh (MUFU tanh.approx: relative error around 2^-11), for values
+// that are rounded to a 16-bit float right after.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The same GELU forms on the hardware tanh: used where the result is stored
+// as bf16 / fp16 (GEMM epilogues, 16-bit element-wise kernels).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  const float u = k0 * fmaf(k1 * x, x * x, x);
+  const float hx = 0.5f * x;
+  return fmaf(hx, tanh_approx(u), hx);
+}
+
+__device__ __forceinline__ float gelu_tanh_grad_fast(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  const float x2 = x * x;
+  const float u = k0 * fmaf(k1 * x2, x, x);
+  const float t = tanh_approx(u);
+  const float du = k0 * fmaf(3.0f * k1, x2, 1.0f);
+  return 0.5f * (1.0f + t) + 0.5f * x * fmaf(-t, t, 1.0f) * du;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -122,14 +122,14 @@ template <typename T>
 __global__ void gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, long long n) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)
-    y[i] = from_f<T>(gelu_tanh(to_f(x[i])));
+    y[i] = from_f<T>(sizeof(T) == 4 ? gelu_tanh(to_f(x[i])) : gelu_tanh_fast(to_f(x[i])));
 }
 
 template <typename T>
 __global__ void gelu_bwd_kernel(const T* __restrict__ x, const T* __restrict__ dy, T* __restrict__ dx, long long n) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)
-    dx[i] = from_f<T>(to_f(dy[i]) * gelu_tanh_grad(to_f(x[i])));
+    dx[i] = from_f<T>(to_f(dy[i]) * (sizeof(T) == 4 ? gelu_tanh_grad(to_f(x[i])) : gelu_tanh_grad_fast(to_f(x[i]))));
 }
 
 constexpr int kReduceBlocks = 296;

@@ -13,12 +13,14 @@
 // Replaces the reference's cublasSgemm call in CudaTensorF32::matmul
 // (cuda/kernels.cu:488-493) and its Python matmul (tensor.py:609-675).
 //
-// CTA layout (192 threads, one CTA per SM, persistent over tiles):
+// CTA layout (320 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer (one elected lane), 128B-swizzled tiles, no
 //               multicast (this kernel also runs inside multi-GPU jobs)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes each, fused bias / GELU /
-//               residual / dGELU / fp32-accumulate, vectorized stores
+//   warps 2..9  epilogue: tcgen05.ld 32 lanes each (warp % 4 selects the
+//               lane quarter, (warp - 2) / 4 the half of the BN columns),
+//               fused bias / GELU / residual / dGELU / fp32-accumulate,
+//               vectorized stores
 // The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of
 // tile i overlaps the main loop of tile i+1.  Every wait is bounded.
 #include <cudaTypedefs.h>
@@ -37,7 +39,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;           // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // producer, MMA, 8 epilogue warps
 constexpr int kSmemBudget = 200 * 1024;
 
 template <int BN>
@@ -49,6 +51,15 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
 };
+
+// bf16 epilogues stage each warp's 32 x 32 output box in shared memory (64-byte
+// rows, 64-byte swizzle) and write it with one TMA store; fp32 epilogues
+// store directly.
+constexpr int kEpiWarps = 8;
+constexpr int kEpiBox = 32 * 32 * 2;
+__host__ __device__ constexpr int epi_boxes(int epi) {
+  return epi == GEMM_EPI_BIAS_GELU ? 2 : ((epi == GEMM_EPI_F32_ACCUM || epi == GEMM_EPI_F32_STORE) ? 0 : 1);
+}
 
 struct GemmArgs {
   int M, N, K;
@@ -121,15 +132,18 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAuxOut,
                         const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   constexpr uint32_t kIdesc = make_idesc(1 /*bf16*/, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
 
+  constexpr int kBoxes = epi_boxes(EPI);
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint8_t* tiles = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* epi_stage = smem + S * Cfg::kStageBytes;  // [kEpiWarps][kBoxes] boxes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + kEpiWarps * kBoxes * kEpiBox);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -143,13 +157,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (kBoxes > 0) tma_prefetch_desc(&tmC);
+    if constexpr (kBoxes > 1) tma_prefetch_desc(&tmAuxOut);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 256);
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -268,7 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;        // TMEM lane quarter this warp may access
+    const int ehalf = (warp - 2) >> 2;   // which half of the BN columns
+    uint8_t* box = epi_stage + (warp - 2) * kBoxes * kEpiBox;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_units; t += gridDim.x) {
@@ -279,14 +297,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
       const bool row_ok = row < args.M;
+      const int c_begin = ehalf * (BN / 64), c_end = min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c_begin; c < c_end; ++c) {
         const int col0 = n0 + c * 32;
-        if (col0 >= args.N) break;  // warp-uniform
         float v[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32);
         tmem_ld_32x32b_x32(taddr, v);
         tc_wait_ld();
+        if (c == c_end - 1) {
+          // the whole accumulator of this warp is in registers: release it
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
         const int valid = min(32, args.N - col0);
         if constexpr (EPI == GEMM_EPI_BF16 || EPI == GEMM_EPI_BIAS_GELU || EPI == GEMM_EPI_RESID) {
           if (args.bias != nullptr) {
@@ -296,46 +319,78 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) v[j] += b[j];
           }
         }
-        if (!row_ok) continue;
-        if constexpr (EPI == GEMM_EPI_BF16) {
-          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
-        } else if constexpr (EPI == GEMM_EPI_BIAS_GELU) {
-          store_bf16x32(args.aux_out + (long long)row * args.ld_aux_out + col0, v, valid);
+        if constexpr (EPI == GEMM_EPI_RESID) {
+          if (row_ok) {
+            float r[32];
+            load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
-        } else if constexpr (EPI == GEMM_EPI_RESID) {
-          float r[32];
-          load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += r[j];
-          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+            for (int j = 0; j < 32; ++j) v[j] += r[j];
+          }
         } else if constexpr (EPI == GEMM_EPI_DGELU) {
-          float u[32];
-          load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
+          if (row_ok) {
+            float u[32];
+            load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad(u[j]);
-          store_bf16x32(reinterpret_cast<__nv_bfloat16*>(args.C) + (long long)row * args.ldc + col0, v, valid);
+            for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad_fast(u[j]);
+          }
+        }
+        if constexpr (kBoxes > 0) {
+          // row `lane` of the warp's box: 4 chunks of 16 B at chunk ^ ((lane >> 1) & 3)
+          if (lane == 0) bulk_wait_group_read0();  // the previous stores have read the boxes
+          __syncwarp();
+          uint8_t* brow = box + lane * 64;
+          const int sw = (lane >> 1) & 3;
+          if constexpr (EPI == GEMM_EPI_BIAS_GELU) {
+            uint8_t* arow = brow + kEpiBox;  // pre-activation box (kept for the backward pass)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(arow + ((q ^ sw) << 4)) =
+                  make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                             pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(brow + ((q ^ sw) << 4)) =
+                make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                           pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            // rows >= M and columns >= N fall outside the tensor map and are not written
+            tma_store_2d(&tmC, box, col0, m0 + quarter * 32);
+            if constexpr (EPI == GEMM_EPI_BIAS_GELU) tma_store_2d(&tmAuxOut, box + kEpiBox, col0, m0 + quarter * 32);
+            bulk_commit_group();
+          }
         } else if constexpr (EPI == GEMM_EPI_F32_ACCUM) {
-          float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+          if (row_ok) {
+            float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (q * 4 < valid)
-              atomicAdd(reinterpret_cast<float4*>(dst + q * 4), make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+            for (int q = 0; q < 8; ++q)
+              if (q * 4 < valid) red_add_f32x4(dst + q * 4, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          }
         } else {  // GEMM_EPI_F32_STORE
-          float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+          if (row_ok) {
+            float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (q * 4 < valid)
-              *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            for (int q = 0; q < 8; ++q)
+              if (q * 4 < valid)
+                *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (c_begin >= c_end) {  // this warp has no columns in a narrow last tile
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    if constexpr (kBoxes > 0) {
+      if (lane == 0) bulk_wait_group0();
     }
   }
 
@@ -391,13 +446,31 @@ int num_sms() {
   return n;
 }
 
+// 2-D bf16 output map for the epilogue: box of 32 columns x 32 rows, 64-byte swizzle.
+CUtensorMap make_out_tmap(const void* base, uint64_t cols, uint64_t rows, uint64_t row_stride_elems) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("gemm output must be 16-byte aligned");
+  if ((row_stride_elems * 2) % 16 != 0) throw std::runtime_error("gemm output stride must be a multiple of 8");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 void launch(const GemmProblem& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
+  constexpr int kSmem = Cfg::kSmemBytes + kEpiWarps * epi_boxes(EPI) * kEpiBox;
+  static_assert(kSmem <= 227 * 1024, "gemm shared memory");
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
-    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     attr_set = true;
   }
   // A: K-major [M][lda] -> dims {K, M}; MN-major [K][lda] -> dims {M, K}
@@ -425,7 +498,10 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   const int units = a.tiles_m * a.tiles_n * a.splits;
   int grid = units < num_sms() ? units : num_sms();
   if (p.max_ctas > 0 && grid > p.max_ctas) grid = p.max_ctas;
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, a);
+  CUtensorMap tc{}, taux{};
+  if constexpr (epi_boxes(EPI) > 0) tc = make_out_tmap(p.C, p.N, p.M, p.ldc);
+  if constexpr (epi_boxes(EPI) > 1) taux = make_out_tmap(p.aux_out, p.N, p.M, p.ld_aux_out);
+  kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, tc, taux, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
