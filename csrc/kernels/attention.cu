@@ -234,44 +234,58 @@ __global__ void __launch_bounds__(256) fa_fwd_kernel(const AttnParams p) {
 }
 
 // --------------------------------------------------------- backward helpers
-// delta[b,h,t] = sum_d dO * O ; dq_accum zeroed.
+// delta[b,h,t] = sum_d dO * O ; dq_accum zeroed.  Eight elements per thread
+// (16-byte loads), D/8 threads per (b, t, h) row.
 template <int D>
-__global__ void fa_bwd_prep_kernel(const AttnBwdParams p) {
-  const int warps = blockDim.x >> 5;
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(256) fa_bwd_prep_kernel(const AttnBwdParams p) {
+  constexpr int TPR = D / 8;  // threads per row
   const long long rows = (long long)p.f.B * p.f.T * p.f.H;
-  for (long long r = blockIdx.x * (long long)warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
+  const int sub = threadIdx.x % TPR;
+  const long long stride = (long long)gridDim.x * (blockDim.x / TPR);
+  for (long long r = blockIdx.x * (long long)(blockDim.x / TPR) + threadIdx.x / TPR; r < rows; r += stride) {
     const int h = r % p.f.H;
     const int tt = (r / p.f.H) % p.f.T;
     const int b = r / ((long long)p.f.H * p.f.T);
-    const __nv_bfloat16* og = p.f.o + b * p.f.o_stride_b + (long long)tt * p.f.o_stride_t + h * D;
-    const __nv_bfloat16* dg = p.dout + b * p.do_stride_b + (long long)tt * p.do_stride_t + h * D;
+    const uint4 ov = *reinterpret_cast<const uint4*>(p.f.o + b * p.f.o_stride_b + (long long)tt * p.f.o_stride_t +
+                                                     h * D + sub * 8);
+    const uint4 dv = *reinterpret_cast<const uint4*>(p.dout + b * p.do_stride_b + (long long)tt * p.do_stride_t +
+                                                     h * D + sub * 8);
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
     float acc = 0.f;
-    for (int d = lane * 2; d < D; d += 64) {
-      float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(og + d));
-      float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(dg + d));
-      acc += a.x * c.x + a.y * c.y;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = __bfloat1622float2(o2[e]), c = __bfloat1622float2(d2[e]);
+      acc = fmaf(a.x, c.x, fmaf(a.y, c.y, acc));
     }
-    acc = warp_sum(acc);
-    if (lane == 0) p.delta[((long long)b * p.f.H + h) * p.f.T + tt] = acc;
-    float* dq = p.dq_accum + r * D;
-    for (int d = lane * 4; d < D; d += 128) *reinterpret_cast<float4*>(dq + d) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int o = TPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (sub == 0) p.delta[((long long)b * p.f.H + h) * p.f.T + tt] = acc;
+    float4* dq = reinterpret_cast<float4*>(p.dq_accum + r * D + sub * 8);
+    dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
+// dq (bf16, strided into the fused gradient) = scale * dq_accum; 8 elements per thread.
 template <int D>
-__global__ void fa_bwd_dq_convert_kernel(const AttnBwdParams p) {
-  const long long total = (long long)p.f.B * p.f.T * p.f.H * (D / 2);
+__global__ void __launch_bounds__(256) fa_bwd_dq_convert_kernel(const AttnBwdParams p) {
+  const long long total = (long long)p.f.B * p.f.T * p.f.H * (D / 8);
   const float sc = p.f.scale;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int d2 = (i % (D / 2)) * 2;
-    const long long r = i / (D / 2);
+    const int d8 = (int)(i % (D / 8)) * 8;
+    const long long r = i / (D / 8);
     const int h = r % p.f.H;
     const int tt = (r / p.f.H) % p.f.T;
     const int b = r / ((long long)p.f.H * p.f.T);
-    float2 v = *reinterpret_cast<const float2*>(p.dq_accum + r * D + d2);
-    __nv_bfloat16* dst = p.dq + b * p.dq_stride_b + (long long)tt * p.dq_stride_t + h * D + d2;
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16(v.x * sc, v.y * sc);
+    const float4* src = reinterpret_cast<const float4*>(p.dq_accum + r * D + d8);
+    const float4 x = src[0], y = src[1];
+    uint4 out;
+    out.x = pack_bf16(x.x * sc, x.y * sc);
+    out.y = pack_bf16(x.z * sc, x.w * sc);
+    out.z = pack_bf16(y.x * sc, y.y * sc);
+    out.w = pack_bf16(y.z * sc, y.w * sc);
+    *reinterpret_cast<uint4*>(p.dq + b * p.dq_stride_b + (long long)tt * p.dq_stride_t + h * D + d8) = out;
   }
 }
 
@@ -505,7 +519,8 @@ void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
     set = true;
   }
   const long long rows = (long long)p.f.B * p.f.T * p.f.H;
-  int g1 = (int)((rows + 7) / 8);
+  const long long rows_per_block = 256 / (D / 8);
+  int g1 = (int)((rows + rows_per_block - 1) / rows_per_block);
   if (g1 > 148 * 16) g1 = 148 * 16;
   fa_bwd_prep_kernel<D><<<g1, 256, 0, s>>>(p);
   note_launch();
@@ -520,7 +535,7 @@ void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
     fa_bwd_kernel<D><<<grid, 128, smem, s>>>(p);
     note_launch();
   }
-  long long tot = rows * (D / 2);
+  long long tot = rows * (D / 8);
   int g2 = (int)((tot + 255) / 256);
   if (g2 > 148 * 16) g2 = 148 * 16;
   fa_bwd_dq_convert_kernel<D><<<g2, 256, 0, s>>>(p);
@@ -547,6 +562,12 @@ void flash_attn_fwd(const AttnParams& p, cudaStream_t s) {
 
 void flash_attn_bwd(const AttnBwdParams& p, cudaStream_t s) {
   if (p.f.T <= 0 || p.f.B <= 0 || p.f.H <= 0) return;
+  // the delta / dQ helper kernels move 8 elements per 16-byte access
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!al16(p.f.o) || !al16(p.dout) || !al16(p.dq) || !al16(p.dq_accum) || p.f.o_stride_t % 8 != 0 ||
+      p.f.o_stride_b % 8 != 0 || p.do_stride_t % 8 != 0 || p.do_stride_b % 8 != 0 || p.dq_stride_t % 8 != 0 ||
+      p.dq_stride_b % 8 != 0)
+    throw std::runtime_error("flash attention backward: o / dout / dq need 16-byte aligned rows");
   if (p.f.D == 64) bwd_impl<64>(p, s);
   else if (p.f.D == 128) bwd_impl<128>(p, s);
   else throw std::runtime_error("flash attention supports head_dim 64 or 128");

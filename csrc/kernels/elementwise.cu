@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256) colsum_vec_kernel(const __nv_bfloat16* __
   const int r1 = min(rows, r0 + rows_per_block);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (c0 < cols) {
-#pragma unroll 4
+#pragma unroll 8
     for (int r = r0 + warp; r < r1; r += 8) {
       uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + (long long)r * ld + c0));
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -376,7 +376,9 @@ void colsum_accum(const __nv_bfloat16* x, long long ld, float* out, int rows, in
   if (rows <= 0 || cols <= 0) return;
   if (cols % 8 == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
     const int gx = (cols + 255) / 256;
-    int gy = (2 * 148 + gx - 1) / gx;
+    // ~8 blocks (64 warps) per SM keep enough loads in flight, but at most 64
+    // blocks per column range so the per-column atomics do not serialise in L2
+    int gy = min(64, (8 * 148 + gx - 1) / gx);
     int rpb = (rows + gy - 1) / gy;
     rpb = (rpb + 7) / 8 * 8;
     gy = (rows + rpb - 1) / rpb;

@@ -32,7 +32,8 @@ struct GemmProblem {
   long long ld_aux = 0;
   __nv_bfloat16* aux_out = nullptr;
   long long ld_aux_out = 0;
-  int splits = 1;     // split-K factor (only meaningful with GEMM_EPI_F32_ACCUM)
+  int splits = 1;     // split-K factor (GEMM_EPI_F32_ACCUM only); 0 = stream-K (equal k-block
+                      // ranges per CTA, partial tiles accumulated by the fp32 epilogue)
   int block_n = 0;    // 0 = choose, else 128 or 256
   int max_ctas = 0;   // 0 = one per SM
 };

@@ -64,6 +64,7 @@ __host__ __device__ constexpr int epi_boxes(int epi) {
 struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, splits, kb_per_split, kb_total;
+  int stream_k;  // fp32-accumulate only: CTAs take equal contiguous (tile, k-block) ranges
   void* C;
   long long ldc;
   const __nv_bfloat16* bias;
@@ -73,6 +74,43 @@ struct GemmArgs {
   long long ld_aux_out;
   DeviceStatus* status;
 };
+
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, int& tn, int& split);
+
+// Work units of one CTA, identical in the producer, MMA and epilogue roles.
+//   tiled:    units blockIdx.x, +gridDim.x, ... of tiles_m * tiles_n * splits
+//   stream-K: the k-block range [b*W/G, (b+1)*W/G) of the W = tiles * kb_total
+//             linearised (tile, k-block) space, cut at tile boundaries; each
+//             piece is accumulated into C by the fp32 epilogue.
+struct UnitIter {
+  long long pos, end;
+};
+
+__device__ __forceinline__ UnitIter unit_begin(const GemmArgs& a) {
+  if (a.stream_k) {
+    const long long total = (long long)a.tiles_m * a.tiles_n * a.kb_total;
+    return {(long long)blockIdx.x * total / gridDim.x, (long long)(blockIdx.x + 1) * total / gridDim.x};
+  }
+  return {(long long)blockIdx.x, (long long)a.tiles_m * a.tiles_n * a.splits};
+}
+
+__device__ __forceinline__ bool unit_next(const GemmArgs& a, UnitIter& it, int& tm, int& tn, int& kb0, int& kb1) {
+  if (it.pos >= it.end) return false;
+  int split;
+  if (a.stream_k) {
+    const int tile = (int)(it.pos / a.kb_total);
+    kb0 = (int)(it.pos - (long long)tile * a.kb_total);
+    kb1 = (int)min((long long)a.kb_total, kb0 + (it.end - it.pos));
+    it.pos += kb1 - kb0;
+    tile_coords(a, tile, tm, tn, split);
+    return true;
+  }
+  tile_coords(a, (int)it.pos, tm, tn, split);
+  kb0 = split * a.kb_per_split;
+  kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+  it.pos += gridDim.x;
+  return true;
+}
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, int& tn, int& split) {
   const int mn_tiles = a.tiles_m * a.tiles_n;
@@ -180,8 +218,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_units = args.tiles_m * args.tiles_n * args.splits;
-
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
@@ -189,12 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x) {
-        int tm, tn, split;
-        tile_coords(args, t, tm, tn, split);
+      UnitIter it = unit_begin(args);
+      int tm, tn, kb0, kb1;
+      while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * BM, n0 = tn * BN;
-        const int kb0 = split * args.kb_per_split;
-        const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.status, kErrWaitTimeoutEmpty, 10)) {
             ok = false;
@@ -236,11 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_units && ok; t += gridDim.x) {
-        int tm, tn, split;
-        tile_coords(args, t, tm, tn, split);
-        const int kb0 = split * args.kb_per_split;
-        const int kb1 = min(kb0 + args.kb_per_split, args.kb_total);
+      UnitIter it = unit_begin(args);
+      int tm, tn, kb0, kb1;
+      while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 20)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -289,9 +321,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* box = epi_stage + (warp - 2) * kBoxes * kEpiBox;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_units; t += gridDim.x) {
-      int tm, tn, split;
-      tile_coords(args, t, tm, tn, split);
+    UnitIter it = unit_begin(args);
+    int tm, tn, kb0, kb1;
+    while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * BM, n0 = tn * BN;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
       tc_fence_after();
@@ -483,6 +515,8 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   a.tiles_m = (p.M + BM - 1) / BM;
   a.tiles_n = (p.N + BN - 1) / BN;
   a.kb_total = (p.K + BK - 1) / BK;
+  // splits == 0 with the fp32-accumulate epilogue selects stream-K
+  a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
   int splits = p.splits < 1 ? 1 : p.splits;
   if (splits > a.kb_total) splits = a.kb_total;
   a.kb_per_split = (a.kb_total + splits - 1) / splits;
@@ -495,8 +529,9 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   a.aux_out = p.aux_out;
   a.ld_aux_out = p.ld_aux_out;
   a.status = device_status_ptr();
-  const int units = a.tiles_m * a.tiles_n * a.splits;
-  int grid = units < num_sms() ? units : num_sms();
+  const long long units = a.stream_k ? (long long)a.tiles_m * a.tiles_n * a.kb_total
+                                     : (long long)a.tiles_m * a.tiles_n * a.splits;
+  int grid = units < num_sms() ? (int)units : num_sms();
   if (p.max_ctas > 0 && grid > p.max_ctas) grid = p.max_ctas;
   CUtensorMap tc{}, taux{};
   if constexpr (epi_boxes(EPI) > 0) tc = make_out_tmap(p.C, p.N, p.M, p.ldc);

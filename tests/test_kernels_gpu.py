@@ -69,8 +69,10 @@ def test_gemm_dgrad_wgrad(K, M, N, K_):
     K.linear_wgrad_accum(dy, x, dw)
     ref = dy.float().t() @ x.float()
     assert O.rel_err(dw, ref) < 1e-2
-    K.linear_wgrad_accum(dy, x, dw)  # accumulates
+    K.linear_wgrad_accum(dy, x, dw)  # accumulates (stream-K)
     assert O.rel_err(dw, 2 * ref) < 1e-2
+    K.linear_wgrad_accum(dy, x, dw, splits=3)  # classic split-K
+    assert O.rel_err(dw, 3 * ref) < 1e-2
     _status_ok()
 
 

@@ -106,13 +106,19 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, gelu_in: torch.Tensor | None
     return dx
 
 
-def linear_wgrad_accum(dy: torch.Tensor, x: torch.Tensor, dw32: torch.Tensor) -> None:
-    """dw32[N,K] += dy[M,N]^T x[M,K]  (fp32, split-K with atomic accumulation)."""
+def linear_wgrad_accum(dy: torch.Tensor, x: torch.Tensor, dw32: torch.Tensor, splits: int = 0) -> None:
+    """dw32[N,K] += dy[M,N]^T x[M,K]  (fp32, atomic accumulation).
+
+    splits=0 runs stream-K: every CTA takes an equal share of the
+    (tile, k-block) work and accumulates partial tiles, so the grid stays full
+    whatever the tile count; splits>=1 is classic split-K.
+    """
     M, N = dy.shape
     K = x.shape[1]
-    tiles = math.ceil(N / 128) * math.ceil(K / 256)
+    if splits == 0 and math.ceil(N / 128) * math.ceil(K / 256) >= 4 * NUM_SMS:
+        splits = 1  # enough tiles for >= 4 full waves: plain tiles keep better L2 reuse
     gemm_raw(N, K, M, dy, dy.stride(0), True, x, x.stride(0), True, dw32, dw32.stride(0), EPI_F32_ACCUM,
-             splits=_splits_for(tiles, M))
+             splits=splits)
 
 
 def matmul_bf16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
