@@ -1,0 +1,203 @@
+"""Single-kernel workloads for profiling and micro-benchmarking.
+
+    python -m underhfs_b200.kernel_cases <case> [--iters N] [--time]
+
+Each case builds its inputs once, launches one native kernel (or one fused
+op) ``--iters`` times and checks the device status word.  Sizes are chosen
+so the operands are larger than the 126 MB L2 where the kernel is
+memory-bound, while the whole case stays at a few GB of device memory, which
+keeps an ``ncu --set full`` capture of one launch short.  ``--time`` prints
+the CUDA-event time per launch after three warm-up launches.
+
+Shapes follow the 125M TransformerLM step (16 x 1024 tokens, d_model 768,
+12 heads of 64, MLP 3072, vocab 32000) unless the case says otherwise.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+from typing import Callable
+
+import torch
+
+from underhfs_b200.ops import kernels as K
+
+TOKENS = 16 * 1024
+
+
+def _bf(*shape: int, scale: float = 1.0) -> torch.Tensor:
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+def _case_gemm_fwd():
+    x, w = _bf(TOKENS, 768), _bf(2304, 768, scale=0.03)
+    return lambda: K.linear_fwd(x, w), 2.0 * TOKENS * 2304 * 768, 0
+
+
+def _case_gemm_fwd_gelu():
+    x, w, b = _bf(TOKENS, 768), _bf(3072, 768, scale=0.03), _bf(3072)
+    return lambda: K.linear_fwd_gelu(x, w, b), 2.0 * TOKENS * 3072 * 768, 0
+
+
+def _case_gemm_dgrad_dgelu():
+    dy, w, u = _bf(TOKENS, 768), _bf(768, 3072, scale=0.03), _bf(TOKENS, 3072)
+    return lambda: K.linear_dgrad(dy, w, gelu_in=u), 2.0 * TOKENS * 3072 * 768, 0
+
+
+def _case_gemm_wgrad():
+    dy, x = _bf(TOKENS, 2304), _bf(TOKENS, 768)
+    dw = torch.zeros(2304, 768, device="cuda")
+    return lambda: K.linear_wgrad_accum(dy, x, dw), 2.0 * TOKENS * 2304 * 768, 0
+
+
+def _case_gemm_8192():
+    a, b = _bf(8192, 8192, scale=0.02), _bf(8192, 8192, scale=0.02)
+    return lambda: K.linear_fwd(a, b), 2.0 * 8192 ** 3, 0
+
+
+def _attn_inputs(B=4, T=1024, H=12, D=64):
+    qkv = _bf(B * T, 3 * H * D)
+    o, lse = K.flash_attn_qkv(qkv, B, T, H, D, True)
+    return qkv, o, lse, (B, T, H, D)
+
+
+def _case_attn_fwd():
+    qkv, _, _, (B, T, H, D) = _attn_inputs()
+    return lambda: K.flash_attn_qkv(qkv, B, T, H, D, True), 2.0 * B * H * T * T * D, 0
+
+
+def _case_attn_bwd():
+    qkv, o, lse, (B, T, H, D) = _attn_inputs()
+    do = _bf(B * T, H * D)
+    return (lambda: K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, True), 5.0 * B * H * T * T * D, 0)
+
+
+def _case_rmsnorm_fwd():
+    x, w = _bf(4 * TOKENS, 768), _bf(768)
+    return lambda: K.rmsnorm(x, w, 1e-8), 0, 2 * x.numel() * 2
+
+
+def _case_rmsnorm_bwd():
+    x, w, dy = _bf(4 * TOKENS, 768), _bf(768), _bf(4 * TOKENS, 768)
+    _, rstd = K.rmsnorm(x, w, 1e-8)
+    dres = _bf(4 * TOKENS, 768)
+    dw = torch.zeros(768, device="cuda")
+    return lambda: K.rmsnorm_backward(dy, x, w, rstd, dres=dres, dw32=dw), 0, 4 * x.numel() * 2
+
+
+def _case_softmax_ce():
+    rows, cols = 4096, 32000
+    logits = _bf(rows, cols)
+    tg = torch.randint(0, cols, (rows,), device="cuda", dtype=torch.int64)
+    dl = torch.empty_like(logits)
+    return lambda: K.softmax_cross_entropy(logits, tg, dl, 1.0 / rows), 0, 2 * logits.numel() * 2
+
+
+def _case_embedding_fwd():
+    tok, pos = _bf(32000, 768), _bf(1024, 768)
+    ids = torch.randint(0, 32000, (4 * TOKENS,), device="cuda", dtype=torch.int64)
+    return lambda: K.embedding(ids, tok, pos, 1024), 0, 2 * ids.numel() * 768 * 2
+
+
+def _case_embedding_bwd():
+    ids = torch.randint(0, 32000, (4 * TOKENS,), device="cuda", dtype=torch.int64)
+    dout = _bf(4 * TOKENS, 768)
+    dtok, dpos = torch.zeros(32000, 768, device="cuda"), torch.zeros(1024, 768, device="cuda")
+    return lambda: K.embedding_backward(ids, dout, dtok, dpos, 1024), 0, dout.numel() * 2
+
+
+def _ew(op: int, dtype: torch.dtype):
+    n = 1 << 26
+    a = torch.randn(n, device="cuda").to(dtype)
+    b = torch.randn(n, device="cuda").to(dtype)
+    return lambda: K.ew_binary(op, a, b), 0, 3 * n * a.element_size()
+
+
+def _case_adamw():
+    n = 32 << 20
+    p32 = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+
+    def run():
+        K.adamw_(p32, g, m, v, p16, lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, decoupled=True)
+
+    return run, 0, n * (4 * 4 + 3 * 4 + 2)
+
+
+def _case_colsum():
+    x = _bf(TOKENS, 3072)
+    out = torch.zeros(3072, device="cuda")
+    return lambda: K.colsum_accum(x, out), 0, x.numel() * 2
+
+
+CASES: dict[str, Callable] = {
+    "gemm_fwd": _case_gemm_fwd,
+    "gemm_fwd_gelu": _case_gemm_fwd_gelu,
+    "gemm_dgrad_dgelu": _case_gemm_dgrad_dgelu,
+    "gemm_wgrad": _case_gemm_wgrad,
+    "gemm_8192": _case_gemm_8192,
+    "attn_fwd": _case_attn_fwd,
+    "attn_bwd": _case_attn_bwd,
+    "rmsnorm_fwd": _case_rmsnorm_fwd,
+    "rmsnorm_bwd": _case_rmsnorm_bwd,
+    "softmax_ce": _case_softmax_ce,
+    "embedding_fwd": _case_embedding_fwd,
+    "embedding_bwd": _case_embedding_bwd,
+    "add_bf16": lambda: _ew(K.OP_ADD, torch.bfloat16),
+    "mul_bf16": lambda: _ew(K.OP_MUL, torch.bfloat16),
+    "add_fp16": lambda: _ew(K.OP_ADD, torch.float16),
+    "mul_fp16": lambda: _ew(K.OP_MUL, torch.float16),
+    "add_fp32": lambda: _ew(K.OP_ADD, torch.float32),
+    "mul_fp32": lambda: _ew(K.OP_MUL, torch.float32),
+    "adamw": _case_adamw,
+    "colsum": _case_colsum,
+}
+
+
+def time_case(fn: Callable[[], object], iters: int = 20) -> float:
+    """Milliseconds per launch, CUDA events on the current stream after 3 warm-ups."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("case", choices=sorted(CASES) + ["all"])
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", action="store_true", help="print CUDA-event time per launch")
+    args = ap.parse_args(argv)
+    torch.manual_seed(0)
+    names = sorted(CASES) if args.case == "all" else [args.case]
+    for name in names:
+        fn, flops, nbytes = CASES[name]()
+        if args.time:
+            ms = time_case(fn)
+            rate = f"{flops / ms / 1e9:.0f} TFLOP/s" if flops else f"{nbytes / ms / 1e6:.0f} GB/s"
+            print(f"{name}: {ms * 1e3:.1f} us/launch, {rate}", flush=True)
+        else:
+            for _ in range(args.iters):
+                fn()
+        torch.cuda.synchronize()
+        st = K.core().device_status(True)
+        if st["code"] != 0:
+            print(f"{name}: device status {st}", file=sys.stderr)
+            return 1
+        del fn
+        torch.cuda.empty_cache()
+    print("ok")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
