@@ -14,7 +14,10 @@
 //                      master / moments) and the all-gather of the updated bf16
 //                      weights, pushed straight into every peer's parameter
 //                      buffer.  One kernel, no intermediate buffers.
-//   * allgather_bf16   gather of equal bf16 shards into every rank's buffer.
+//   * allgather        gather of equal shards (any dtype) into every rank's buffer.
+//   * allreduce (bf16) and reduce_scatter (fp32 / bf16): the same peer-load /
+//                      peer-store scheme for bf16 buffers (fp32 accumulation)
+//                      and for a sharded result.
 //
 // Synchronisation: per-(launch, block) epoch flags in an IPC-shared signal
 // pad.  Block b of every rank signals block b of every peer with a
@@ -106,50 +109,138 @@ __device__ __forceinline__ void commit_epoch(const PeerPtrs& pp, int rank, uint3
 struct ArArgs {
   PeerPtrs pp;
   long long off_bytes;  // offset of the bucket inside every rank's data region
-  long long n;          // fp32 elements (multiple of 4)
+  long long n;          // elements (16-byte multiple)
   float scale;
   int rank, world;
   DeviceStatus* status;
 };
 
-__global__ void __launch_bounds__(512) allreduce_f32_kernel(const ArArgs a) {
+// 16-byte vectors: 4 fp32 or 8 bf16, accumulated in fp32.
+template <bool BF16>
+__device__ __forceinline__ void accum16(float (&acc)[8], const uint4 raw) {
+  if constexpr (BF16) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
+    }
+  } else {
+    acc[0] += __uint_as_float(raw.x);
+    acc[1] += __uint_as_float(raw.y);
+    acc[2] += __uint_as_float(raw.z);
+    acc[3] += __uint_as_float(raw.w);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint4 pack16(const float (&acc)[8], float scale) {
+  uint4 r;
+  if constexpr (BF16) {
+    r.x = pack_bf16x2(acc[0] * scale, acc[1] * scale);
+    r.y = pack_bf16x2(acc[2] * scale, acc[3] * scale);
+    r.z = pack_bf16x2(acc[4] * scale, acc[5] * scale);
+    r.w = pack_bf16x2(acc[6] * scale, acc[7] * scale);
+  } else {
+    r = make_uint4(__float_as_uint(acc[0] * scale), __float_as_uint(acc[1] * scale),
+                   __float_as_uint(acc[2] * scale), __float_as_uint(acc[3] * scale));
+  }
+  return r;
+}
+
+// Peer loads are latency-bound (request / response over NVLink), so every
+// thread keeps kUnroll 16-byte vectors per peer in flight.
+constexpr int kUnroll = 4;
+constexpr int kCommThreads = 256;
+
+// In-place two-shot all-reduce: this rank reduces its 1/W slice of the
+// 16-byte vectors from every peer, scales it and stores it back to every peer.
+template <bool BF16>
+__global__ void __launch_bounds__(kCommThreads) allreduce_kernel(const ArArgs a) {
   const uint32_t e = next_epoch(a.pp, a.rank);
   if (!block_barrier(a.pp, a.rank, a.world, kInOff, e, a.status, 100)) {
     commit_epoch(a.pp, a.rank, e);
     return;
   }
-  const long long n4 = a.n / 4;
-  const long long per = (n4 + a.world - 1) / a.world;
+  const long long n16 = a.n / (BF16 ? 8 : 4);
+  const long long per = (n16 + a.world - 1) / a.world;
   const long long lo = per * a.rank;
-  const long long hi = min(n4, lo + per);
-  float4* src[kMaxWorld];
+  const long long hi = min(n16, lo + per);
+  const long long G = (long long)gridDim.x * blockDim.x;
+  for (long long base = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; base < hi; base += kUnroll * G) {
+    uint4 v[kUnroll][kMaxWorld];
 #pragma unroll
-  for (int p = 0; p < kMaxWorld; ++p)
-    src[p] = p < a.world ? reinterpret_cast<float4*>(a.pp.data[p] + a.off_bytes) : nullptr;
-  for (long long i = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < hi;
-       i += (long long)gridDim.x * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 v[kMaxWorld];
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * G;
 #pragma unroll
-    for (int p = 0; p < kMaxWorld; ++p)
-      if (p < a.world) v[p] = __ldcg(src[p] + i);
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world && i < hi) v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.off_bytes) + i);
+    }
 #pragma unroll
-    for (int p = 0; p < kMaxWorld; ++p)
-      if (p < a.world) {
-        acc.x += v[p].x;
-        acc.y += v[p].y;
-        acc.z += v[p].z;
-        acc.w += v[p].w;
-      }
-    acc.x *= a.scale;
-    acc.y *= a.scale;
-    acc.z *= a.scale;
-    acc.w *= a.scale;
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * G;
+      if (i >= hi) break;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int p = 0; p < kMaxWorld; ++p)
-      if (p < a.world) __stcg(src[p] + i, acc);
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world) accum16<BF16>(acc, v[u][p]);
+      const uint4 r = pack16<BF16>(acc, a.scale);
+#pragma unroll
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world) __stcg(reinterpret_cast<uint4*>(a.pp.data[p] + a.off_bytes) + i, r);
+    }
   }
   block_barrier(a.pp, a.rank, a.world, kOutOff, e, a.status, 101);
+  commit_epoch(a.pp, a.rank, e);
+}
+
+struct RsArgs {
+  PeerPtrs pp;
+  long long in_off_bytes;   // [n] input on every rank
+  long long out_off_bytes;  // [n / world] output in this rank's region
+  long long n;              // elements; n / world is a 16-byte multiple
+  float scale;
+  int rank, world;
+  DeviceStatus* status;
+};
+
+// Reduce-scatter: rank r reads shard r of the input from every peer and
+// writes the scaled sum to its own output.  The closing barrier keeps every
+// input alive until all peers have read it.
+template <bool BF16>
+__global__ void __launch_bounds__(kCommThreads) reduce_scatter_kernel(const RsArgs a) {
+  const uint32_t e = next_epoch(a.pp, a.rank);
+  if (!block_barrier(a.pp, a.rank, a.world, kInOff, e, a.status, 140)) {
+    commit_epoch(a.pp, a.rank, e);
+    return;
+  }
+  const long long shard16 = a.n / a.world / (BF16 ? 8 : 4);
+  const long long lo = shard16 * a.rank;
+  uint4* out = reinterpret_cast<uint4*>(a.pp.data[a.rank] + a.out_off_bytes);
+  const long long G = (long long)gridDim.x * blockDim.x;
+  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < shard16; base += kUnroll * G) {
+    uint4 v[kUnroll][kMaxWorld];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * G;
+#pragma unroll
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world && i < shard16)
+          v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.in_off_bytes) + lo + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long i = base + u * G;
+      if (i >= shard16) break;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kMaxWorld; ++p)
+        if (p < a.world) accum16<BF16>(acc, v[u][p]);
+      __stcg(out + i, pack16<BF16>(acc, a.scale));
+    }
+  }
+  block_barrier(a.pp, a.rank, a.world, kOutOff, e, a.status, 141);
   commit_epoch(a.pp, a.rank, e);
 }
 
@@ -338,9 +429,10 @@ static PeerPtrs peer_ptrs(const SymmetricHeap& h) {
 
 static int clamp_blocks(int blocks) { return blocks < 1 ? 1 : (blocks > kMaxBlocks ? kMaxBlocks : blocks); }
 
-void comm_allreduce_f32(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
-                        cudaStream_t s) {
-  if (n % 4 != 0 || off_bytes % 16 != 0) throw std::invalid_argument("allreduce needs 16-byte aligned float4 spans");
+static void launch_allreduce(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
+                             bool bf16, cudaStream_t s) {
+  if (n % (bf16 ? 8 : 4) != 0 || off_bytes % 16 != 0)
+    throw std::invalid_argument("allreduce needs 16-byte aligned spans of whole 16-byte vectors");
   if (n <= 0) return;
   ArArgs a{};
   a.pp = peer_ptrs(h);
@@ -350,7 +442,39 @@ void comm_allreduce_f32(const SymmetricHeap& h, long long off_bytes, long long n
   a.rank = h.rank();
   a.world = h.world();
   a.status = device_status_ptr();
-  allreduce_f32_kernel<<<clamp_blocks(blocks), 512, 0, s>>>(a);
+  if (bf16) allreduce_kernel<true><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  else allreduce_kernel<false><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void comm_allreduce_f32(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
+                        cudaStream_t s) {
+  launch_allreduce(h, off_bytes, n, scale, blocks, false, s);
+}
+
+void comm_allreduce_bf16(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
+                         cudaStream_t s) {
+  launch_allreduce(h, off_bytes, n, scale, blocks, true, s);
+}
+
+void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long long out_off_bytes, long long n,
+                         bool bf16, float scale, int blocks, cudaStream_t s) {
+  const int vec = bf16 ? 8 : 4;
+  if (n <= 0) return;
+  if (n % ((long long)h.world() * vec) != 0 || in_off_bytes % 16 != 0 || out_off_bytes % 16 != 0)
+    throw std::invalid_argument("reduce_scatter needs 16-byte aligned shards of whole 16-byte vectors");
+  RsArgs a{};
+  a.pp = peer_ptrs(h);
+  a.in_off_bytes = in_off_bytes;
+  a.out_off_bytes = out_off_bytes;
+  a.n = n;
+  a.scale = scale;
+  a.rank = h.rank();
+  a.world = h.world();
+  a.status = device_status_ptr();
+  if (bf16) reduce_scatter_kernel<true><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  else reduce_scatter_kernel<false><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

@@ -44,6 +44,10 @@ void comm_rs_adamw_ag(const SymmetricHeap& grads, long long g_off_bytes, const S
                       uintptr_t v, float lr, float beta1, float beta2, float eps, float weight_decay,
                       float grad_scale, bool decoupled, uintptr_t step_ptr, int blocks, cudaStream_t s);
 void comm_allgather(const SymmetricHeap& h, long long off_bytes, long long shard_bytes, int blocks, cudaStream_t s);
+void comm_allreduce_bf16(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
+                         cudaStream_t s);
+void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long long out_off_bytes, long long n,
+                         bool bf16, float scale, int blocks, cudaStream_t s);
 void comm_barrier(const SymmetricHeap& h, cudaStream_t s);
 void comm_wait_probe(const SymmetricHeap& h, unsigned int want, unsigned long long bound_ns, cudaStream_t s);
 

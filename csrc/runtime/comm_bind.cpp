@@ -110,6 +110,12 @@ void bind_comm(py::module_& m) {
   m.def("comm_allgather", [](const SymmetricHeap& h, long long off, long long shard_bytes, int blocks, uintptr_t s) {
     comm_allgather(h, off, shard_bytes, blocks, S(s));
   });
+  m.def("comm_allreduce_bf16", [](const SymmetricHeap& h, long long off, long long n, float scale, int blocks,
+                                  uintptr_t s) { comm_allreduce_bf16(h, off, n, scale, blocks, S(s)); });
+  m.def("comm_reduce_scatter", [](const SymmetricHeap& h, long long in_off, long long out_off, long long n, bool bf16,
+                                  float scale, int blocks, uintptr_t s) {
+    comm_reduce_scatter(h, in_off, out_off, n, bf16, scale, blocks, S(s));
+  });
   m.def("comm_barrier", [](const SymmetricHeap& h, uintptr_t s) { comm_barrier(h, S(s)); });
   m.def("comm_wait_probe", [](const SymmetricHeap& h, unsigned int want, unsigned long long bound_ns, uintptr_t s) {
     comm_wait_probe(h, want, bound_ns, S(s));

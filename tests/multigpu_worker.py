@@ -100,7 +100,10 @@ def case_zero(rank: int, world: int) -> None:
     gen = torch.Generator().manual_seed(200 + rank)
     ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
     tg = torch.roll(ids, -1, 1)
-    kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, decoupled=True)
+    # eps well above the gradient noise: AdamW's first steps move every weight by
+    # ~lr * sign(g), so with eps=1e-8 a near-zero gradient whose fp32 sum order
+    # differs (atomic weight-gradient accumulation) flips a whole 2*lr step
+    kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
     ref_model = _model()
     ref_opt = FusedAdamW(ref_model.parameters(), **kw)
     model = _model()

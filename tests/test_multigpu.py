@@ -31,4 +31,8 @@ def test_two_gpu_case(case):
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            str(ROOT / "tests" / "multigpu_worker.py"), case]
     proc = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
-    assert proc.returncode == 0 and f"OK {case}" in proc.stdout, (proc.stdout[-3000:], proc.stderr[-6000:])
+    if proc.returncode != 0 or f"OK {case}" not in proc.stdout:
+        # shown by pytest under "Captured stdout call"
+        print(proc.stdout[-4000:])
+        print(proc.stderr[-12000:])
+    assert proc.returncode == 0 and f"OK {case}" in proc.stdout, f"worker {case} exited {proc.returncode}"
