@@ -7,6 +7,7 @@
 // embedding) or one CTA (cross-entropy over a 32K vocabulary) owns a row; all
 // loads are 16-byte vectors, statistics are fp32, and the cross-entropy kernel
 // emits the logits gradient in the same pass that computes the loss.
+#include <type_traits>
 #include <stdexcept>
 
 #include "kernels.h"
@@ -17,6 +18,42 @@ namespace uhfs {
 namespace {
 
 bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 8 x 16-bit <-> 8 x fp32 on the register words (no address-taken temporaries).
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    lo = __uint_as_float(w << 16);  // bf16 -> fp32 is exact: the high half of the word
+    hi = __uint_as_float(w & 0xffff0000u);
+  } else {
+    lo = __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+    hi = __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4 raw, float (&f)[8]) {
+  unpack2<T>(raw.x, f[0], f[1]);
+  unpack2<T>(raw.y, f[2], f[3]);
+  unpack2<T>(raw.z, f[4], f[5]);
+  unpack2<T>(raw.w, f[6], f[7]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+}
 
 // ------------------------------------------------------------------ RMSNorm
 template <typename T>
@@ -44,6 +81,54 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict_
 #pragma unroll
       for (int i = 0; i < 8; ++i) f[i] = f[i] * r * g[i];
       store8_guard<T>(yr + c, f, c, cols, vec);
+    }
+  }
+}
+
+// 16-bit rows of cols <= 256 * VPL (cols % 8 == 0): the warp keeps its row
+// slice in registers, so x is read once.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_reg_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                              T* __restrict__ y, float* __restrict__ rstd, int rows,
+                                                              int cols, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float wv[VPL][8];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) {
+    const int c = (v * 32 + lane) * 8;
+    if (c < cols) unpack8<T>(*reinterpret_cast<const uint4*>(w + c), wv[v]);
+  }
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    const long long off = (long long)row * cols;
+    uint4 rx[VPL];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (v * 32 + lane) * 8;
+      if (c < cols) rx[v] = __ldcs(reinterpret_cast<const uint4*>(x + off + c));
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      if ((v * 32 + lane) * 8 < cols) {
+        float f[8];
+        unpack8<T>(rx[v], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)cols + eps);
+    if (lane == 0 && rstd != nullptr) rstd[row] = r;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (v * 32 + lane) * 8;
+      if (c < cols) {
+        float f[8];
+        unpack8<T>(rx[v], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = f[j] * r * wv[v][j];
+        *reinterpret_cast<uint4*>(y + off + c) = pack8<T>(f);
+      }
     }
   }
 }
@@ -84,6 +169,94 @@ __global__ void rmsnorm_bwd_dx_kernel(const T* __restrict__ dy, const T* __restr
       for (int i = 0; i < 8; ++i) o[i] += r * (a[i] * g[i] - b[i] * coef);
       store8_guard<T>(dx + off + c, o, c, cols, vec);
     }
+  }
+}
+
+// One pass for the whole backward (16-bit, cols <= 256 * VPL, cols % 8 == 0):
+// a warp owns a row at a time and keeps its dy / x / dres slices in registers
+// (VPL 16-byte vectors per lane), writes dx, and accumulates the dgamma
+// partials dy * x * r of its columns across all rows it visits; the block
+// combines the 8 warps' partials in shared memory and adds them to dw with
+// one atomic per column.  Reads dy, x, dres once and writes dx once.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                                const T* __restrict__ w,
+                                                                const float* __restrict__ rstd,
+                                                                const T* __restrict__ dres, T* __restrict__ dx,
+                                                                float* __restrict__ dw, int rows, int cols) {
+  __shared__ float part[8][VPL * 256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float wv[VPL][8], acc[VPL][8];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) {
+    const int c = (v * 32 + lane) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[v][j] = 0.f;
+    if (c < cols) unpack8<T>(*reinterpret_cast<const uint4*>(w + c), wv[v]);
+    else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[v][j] = 0.f;
+    }
+  }
+  const float inv_cols = 1.0f / (float)cols;
+  for (int row = blockIdx.x * 8 + warp; row < rows; row += gridDim.x * 8) {
+    const long long off = (long long)row * cols;
+    uint4 rdy[VPL], rx[VPL], rres[VPL];
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (v * 32 + lane) * 8;
+      if (c < cols) {
+        rdy[v] = __ldcs(reinterpret_cast<const uint4*>(dy + off + c));
+        rx[v] = __ldcs(reinterpret_cast<const uint4*>(x + off + c));
+        if (dres != nullptr) rres[v] = __ldcs(reinterpret_cast<const uint4*>(dres + off + c));
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      if ((v * 32 + lane) * 8 < cols) {
+        float a[8], b[8];
+        unpack8<T>(rdy[v], a);
+        unpack8<T>(rx[v], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = fmaf(a[j] * wv[v][j], b[j], dot);
+      }
+    }
+    dot = warp_sum(dot);
+    const float r = rstd[row];
+    const float coef = r * r * dot * inv_cols;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+      const int c = (v * 32 + lane) * 8;
+      if (c < cols) {
+        float a[8], b[8], o[8];
+        unpack8<T>(rdy[v], a);
+        unpack8<T>(rx[v], b);
+        if (dres != nullptr) unpack8<T>(rres[v], o);
+        else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j] += r * (a[j] * wv[v][j] - b[j] * coef);
+          acc[v][j] = fmaf(a[j] * b[j], r, acc[v][j]);
+        }
+        __stcs(reinterpret_cast<uint4*>(dx + off + c), pack8<T>(o));
+      }
+    }
+  }
+  if (dw == nullptr) return;
+#pragma unroll
+  for (int v = 0; v < VPL; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) part[warp][(v * 32 + lane) * 8 + j] = acc[v][j];
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += 256) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) sum += part[w8][c];
+    atomicAdd(dw + c, sum);
   }
 }
 
@@ -207,6 +380,102 @@ __device__ __forceinline__ void online_merge(float& m, float& s, float m2, float
   if (mn == -INFINITY) return;
   s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
   m = mn;
+}
+
+// 16-bit logits, row held in registers: every thread loads its (up to)
+// kCeVecs 16-byte vectors once, so each row is read from memory once and
+// written once (dlogits) -- the minimum traffic.  Block max, then block sum.
+constexpr int kCeVecs = 8;  // rows up to kCeThreads * 8 * kCeVecs = 32768 columns
+
+__device__ __forceinline__ float block_reduce_max(float v, float* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = sm[0];
+#pragma unroll
+  for (int w = 1; w < kCeThreads / 32; ++w) v = fmaxf(v, sm[w]);
+  __syncthreads();
+  return v;
+}
+
+__device__ __forceinline__ float block_reduce_sum(float v, float* sm) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCeThreads / 32; ++w) v += sm[w];
+  __syncthreads();
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* __restrict__ logits, long long ld,
+                                                                      const int64_t* __restrict__ targets,
+                                                                      float* __restrict__ loss_rows, T* dlogits,
+                                                                      int cols, float grad_scale,
+                                                                      const float* grad_scale_ptr) {
+  __shared__ float sm[kCeThreads / 32];
+  const int row = blockIdx.x;
+  const T* lr = logits + (long long)row * ld;
+  const int nvec = cols / 8;
+  uint4 raw[kCeVecs];
+#pragma unroll
+  for (int k = 0; k < kCeVecs; ++k) {
+    const int v = threadIdx.x + k * kCeThreads;
+    if (v < nvec) raw[k] = __ldcs(reinterpret_cast<const uint4*>(lr) + v);  // read once: streaming
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kCeVecs; ++k) {
+    if (threadIdx.x + k * kCeThreads < nvec) {
+      float f[8];
+      unpack8<T>(raw[k], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, f[i]);
+    }
+  }
+  mx = block_reduce_max(mx, sm);
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kCeVecs; ++k) {
+    if (threadIdx.x + k * kCeThreads < nvec) {
+      float f[8];
+      unpack8<T>(raw[k], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum += __expf(f[i] - mx);
+    }
+  }
+  const long long tgt = targets[row];
+  // the target logit is read before the block barrier inside the sum
+  // reduction, so an in-place dlogits (== logits) cannot overwrite it first
+  const float xt = threadIdx.x == 0 ? to_float<T>(lr[tgt]) : 0.f;
+  sum = block_reduce_sum(sum, sm);
+  if (threadIdx.x == 0) {
+    // -log(max(p_t, 1e-30)) as in the reference, computed in log space.
+    const float nll = logf(sum) + mx - xt;
+    loss_rows[row] = fminf(nll, 69.07755279f);
+  }
+  if (dlogits == nullptr) return;
+  if (grad_scale_ptr != nullptr) grad_scale *= *grad_scale_ptr;
+  const float inv = grad_scale / sum;
+  T* dr = dlogits + (long long)row * ld;
+#pragma unroll
+  for (int k = 0; k < kCeVecs; ++k) {
+    const int v = threadIdx.x + k * kCeThreads;
+    if (v < nvec) {
+      float f[8];
+      unpack8<T>(raw[k], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        f[i] = __expf(f[i] - mx) * inv;
+        if ((long long)v * 8 + i == tgt) f[i] -= grad_scale;
+      }
+      __stcs(reinterpret_cast<uint4*>(dr) + v, pack8<T>(f));
+    }
+  }
 }
 
 template <typename T>
@@ -370,6 +639,28 @@ void rmsnorm_fwd(int dtype, const void* x, const void* w, void* y, float* rstd, 
                  cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(x) && al16(w) && al16(y) && (cols % 8 == 0);
+  if (vec && dtype != DT_F32 && cols <= 4 * 256) {
+    int grid = (rows + 7) / 8;
+    if (grid > 8 * 148) grid = 8 * 148;
+    const int vpl = (cols + 255) / 256;
+#define UHFS_RMS_FWD(TT, V)                                                                                      \
+  rmsnorm_fwd_reg_kernel<TT, V><<<grid, 256, 0, s>>>((const TT*)x, (const TT*)w, (TT*)y, rstd, rows, cols, eps)
+    if (dtype == DT_BF16) {
+      if (vpl == 1) UHFS_RMS_FWD(__nv_bfloat16, 1);
+      else if (vpl == 2) UHFS_RMS_FWD(__nv_bfloat16, 2);
+      else if (vpl == 3) UHFS_RMS_FWD(__nv_bfloat16, 3);
+      else UHFS_RMS_FWD(__nv_bfloat16, 4);
+    } else {
+      if (vpl == 1) UHFS_RMS_FWD(__half, 1);
+      else if (vpl == 2) UHFS_RMS_FWD(__half, 2);
+      else if (vpl == 3) UHFS_RMS_FWD(__half, 3);
+      else UHFS_RMS_FWD(__half, 4);
+    }
+#undef UHFS_RMS_FWD
+    note_launch();
+    UHFS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   UHFS_DISPATCH_DTYPE(dtype, rmsnorm_fwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
                                  (const T*)x, (const T*)w, (T*)y, rstd, rows, cols, eps, vec));
   note_launch();
@@ -380,6 +671,30 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
                  void* dx, float* dw_accum, int rows, int cols, cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(dy) && al16(x) && al16(w) && al16(dres) && al16(dx) && (cols % 8 == 0);
+  if (vec && dtype != DT_F32 && cols <= 4 * 256) {
+    // 2 blocks per SM: enough rows in flight, and at most 296 atomics per dgamma column
+    int grid = (rows + 7) / 8;
+    if (grid > 2 * 148) grid = 2 * 148;
+    const int vpl = (cols + 255) / 256;
+#define UHFS_RMS_FUSED(TT, V)                                                                                  \
+  rmsnorm_bwd_fused_kernel<TT, V><<<grid, 256, 0, s>>>((const TT*)dy, (const TT*)x, (const TT*)w, rstd,         \
+                                                      (const TT*)dres, (TT*)dx, dw_accum, rows, cols)
+    if (dtype == DT_BF16) {
+      if (vpl == 1) UHFS_RMS_FUSED(__nv_bfloat16, 1);
+      else if (vpl == 2) UHFS_RMS_FUSED(__nv_bfloat16, 2);
+      else if (vpl == 3) UHFS_RMS_FUSED(__nv_bfloat16, 3);
+      else UHFS_RMS_FUSED(__nv_bfloat16, 4);
+    } else {
+      if (vpl == 1) UHFS_RMS_FUSED(__half, 1);
+      else if (vpl == 2) UHFS_RMS_FUSED(__half, 2);
+      else if (vpl == 3) UHFS_RMS_FUSED(__half, 3);
+      else UHFS_RMS_FUSED(__half, 4);
+    }
+#undef UHFS_RMS_FUSED
+    note_launch();
+    UHFS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dx_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
                                  (const T*)dy, (const T*)x, (const T*)w, rstd, (const T*)dres, (T*)dx, rows, cols, vec));
   note_launch();
@@ -427,6 +742,18 @@ void softmax_ce_fwd_bwd(int dtype, const void* logits, long long ld, const int64
                         cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(logits) && al16(dlogits) && (cols % 8 == 0) && (ld % 8 == 0);
+  if (vec && dtype != DT_F32 && cols <= kCeThreads * 8 * kCeVecs) {
+    if (dtype == DT_BF16)
+      softmax_ce_reg_kernel<__nv_bfloat16><<<rows, kCeThreads, 0, s>>>(
+          (const __nv_bfloat16*)logits, ld, targets, loss_rows, (__nv_bfloat16*)dlogits, cols, grad_scale,
+          grad_scale_ptr);
+    else
+      softmax_ce_reg_kernel<__half><<<rows, kCeThreads, 0, s>>>((const __half*)logits, ld, targets, loss_rows,
+                                                               (__half*)dlogits, cols, grad_scale, grad_scale_ptr);
+    note_launch();
+    UHFS_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   UHFS_DISPATCH_DTYPE(dtype, softmax_ce_kernel<T><<<rows, kCeThreads, 0, s>>>(
                                  (const T*)logits, ld, targets, loss_rows, (T*)dlogits, cols, grad_scale, grad_scale_ptr, vec));
   note_launch();

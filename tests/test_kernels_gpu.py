@@ -104,7 +104,7 @@ def test_elementwise_reduce_cast(K, dtype):
     assert torch.equal(K.ew_binary(K.OP_ADD, odd.contiguous(), odd.contiguous()), (odd.float() * 2).to(dtype))
 
 
-@pytest.mark.parametrize("rows,cols", [(64, 768), (33, 200), (4096, 2048)])
+@pytest.mark.parametrize("rows,cols", [(64, 768), (33, 200), (4096, 2048), (300, 1024), (1000, 512)])
 def test_rmsnorm(K, rows, cols):
     x = bf(torch.randn(rows, cols, device="cuda"))
     w = bf(torch.rand(cols, device="cuda") + 0.5)
@@ -141,7 +141,7 @@ def test_embedding(K):
     assert torch.allclose(dpos, rp, atol=1e-3)
 
 
-@pytest.mark.parametrize("rows,cols", [(8, 32000), (5, 1003)])
+@pytest.mark.parametrize("rows,cols", [(8, 32000), (5, 1003), (3, 50000), (64, 1024)])
 def test_softmax_cross_entropy(K, rows, cols):
     logits = bf(torch.randn(rows, cols, device="cuda") * 3)
     tg = torch.randint(0, cols, (rows,), device="cuda")
