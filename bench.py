@@ -40,6 +40,16 @@ METRIC = "TransformerLM train tokens/sec (device-timed, max over ranks) @1/2/4/8
 MODEL = "125M TransformerLM (d_model 768, 12 layers, 12 heads, MLP 3072, vocab 32000, tied)"
 SEQ, MICRO_BATCH = 1024, 16
 
+# --config: the default is the headline data-parallel run; the others are the
+# larger sharded configurations of the same model family.
+CONFIGS = {
+    "125m-ddp": dict(model="125m", batch=16, seq=1024, zero=0, desc=MODEL),
+    "1.3b-zero2": dict(model="1.3b", batch=8, seq=2048, zero=2,
+                       desc="1.3B TransformerLM (d_model 2048, 24 layers, 16 heads, MLP 8192, vocab 32000, tied)"),
+    "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3,
+                     desc="7B TransformerLM (d_model 4096, 32 layers, 32 heads, MLP 11008, vocab 32000, untied)"),
+}
+
 
 def _clock_sampler(local_rank: int):
     fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -90,8 +100,12 @@ def run_ours(args) -> int:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={n}", file=sys.stderr)
     local = pol.local_rank or 0
     torch.cuda.set_device(local)
-    cfg = TrainConfig(model="125m", batch=MICRO_BATCH, seq_len=SEQ, lr=3e-4, bucket_mb=25.0,
-                      cuda_graph=not args.no_graph)
+    cc = CONFIGS[args.config]
+    if cc["zero"] == 3:
+        return run_zero3(args, pol, cc)
+    cfg = TrainConfig(model=cc["model"], batch=cc["batch"], seq_len=cc["seq"], lr=3e-4, bucket_mb=25.0,
+                      cuda_graph=not args.no_graph, zero_stage=cc["zero"],
+                      decoupled=True, weight_decay=0.0 if cc["zero"] == 0 else 0.1)
     model = build_model(cfg, device=f"cuda:{local}")
     trainer = Trainer(model, cfg, policy=pol)
     src = SyntheticTokens(model.vocab_size, cfg.batch, cfg.seq_len, seed=1234, rank=pol.rank)
@@ -166,10 +180,12 @@ def run_ours(args) -> int:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic uniform token ids in [0,32000) from a fixed seed; random-init weights",
-            "config": {"model": MODEL, "global_batch": n * cfg.batch, "micro_batch_per_gpu": cfg.batch,
-                       "seq_len": cfg.seq_len, "parallelism": f"dp{n}",
-                       "optimizer": "FusedAdamW lr 3e-4 (fp32 master, one fused launch)",
-                       "grad_allreduce": "fused NVLink two-shot kernel, 25 MB buckets overlapped with backward",
+            "config": {"model": cc["desc"], "global_batch": n * cfg.batch, "micro_batch_per_gpu": cfg.batch,
+                       "seq_len": cfg.seq_len, "parallelism": f"dp{n}" if cc["zero"] == 0 else f"zero{cc['zero']}-{n}",
+                       "optimizer": ("FusedAdamW lr 3e-4 (fp32 master, one fused launch)" if cc["zero"] == 0 else
+                                     "ZeRO-2 AdamW: fused NVLink reduce-scatter + AdamW + all-gather kernel"),
+                       "grad_allreduce": ("fused NVLink two-shot kernel, 25 MB buckets overlapped with backward"
+                                          if cc["zero"] == 0 else "reduce-scatter fused with the AdamW update"),
                        "cuda_graph": not args.no_graph,
                        "l2": "no flush: per-step working set (weights, grads, moments, activations) >> 126 MB L2"},
             "clocks": clocks,
@@ -207,6 +223,96 @@ def run_reference(args) -> int:
     return 0
 
 
+def run_zero3(args, pol, cc) -> int:
+    """7B-class ZeRO-3: sharded weights / grads / moments, per-layer gathers and
+    reduce-scatter fused with AdamW (underhfs_b200.parallel.zero3)."""
+    import torch
+    import torch.distributed as dist
+
+    from underhfs_b200.distributed import init_process_group
+    from underhfs_b200.ops._lib import core
+    from underhfs_b200.parallel.zero3 import Zero3LM
+    from underhfs_b200.train import PRESETS
+
+    n, local = pol.world_size, pol.local_rank or 0
+    if n > 1:
+        init_process_group(pol)
+    spec = PRESETS[cc["model"]]
+    z = Zero3LM(spec, rank=pol.rank, world=n, device=f"cuda:{local}", lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
+                weight_decay=0.1, decoupled=True, seed=1234)
+    gen = torch.Generator().manual_seed(1234 + pol.rank)
+    pool = [torch.randint(0, spec.vocab_size, (2, cc["batch"], cc["seq"]), generator=gen).cuda() for _ in range(2)]
+
+    def barrier():
+        if n > 1:
+            dist.barrier()
+
+    c = core()
+    c.reset_launch_count()
+    z.train_step(pool[0][0], pool[0][1])
+    torch.cuda.synchronize()
+    launches_per_step = c.launch_count()
+    for i in range(args.warmup):
+        z.train_step(pool[i % 2][0], pool[i % 2][1])
+    torch.cuda.synchronize()
+    barrier()
+    sampler, clock_path = _clock_sampler(local)
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        loss = z.train_step(pool[i % 2][0], pool[i % 2][1])
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    if sampler is not None:
+        sampler.terminate()
+        sampler.wait()
+    ms = start.elapsed_time(end)
+    final_loss = float(loss.item())
+    host = torch.empty((2, cc["batch"], cc["seq"]), dtype=torch.int64, pin_memory=True)
+    host.copy_(pool[0].cpu())
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dev = host.to(f"cuda:{local}", non_blocking=True)
+        float(z.train_step(dev[0], dev[1]).item())
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    stats = torch.tensor([ms, e2e_s], dtype=torch.float64, device="cuda")
+    if n > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max = stats.tolist()
+    clocks = _clock_summary(clock_path)
+    tokens = n * cc["batch"] * cc["seq"] * args.steps
+    if pol.rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": tokens / (ms_max / 1e3), "unit": "tokens/s", "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic uniform token ids in [0,32000) from a fixed seed; random-init weights",
+            "config": {"model": cc["desc"], "global_batch": n * cc["batch"], "micro_batch_per_gpu": cc["batch"],
+                       "seq_len": cc["seq"], "parallelism": f"zero3-{n}",
+                       "optimizer": "ZeRO-3 AdamW: per-unit reduce-scatter fused with AdamW on owned rows",
+                       "param_gather": "per-unit push all-gather over NVLink, prefetched one unit ahead",
+                       "cuda_graph": False,
+                       "l2": "no flush: per-step working set >> 126 MB L2"},
+            "clocks": clocks,
+            "e2e": {"value": tokens / e2e_max, "unit": "tokens/s",
+                    "h2d_bytes_per_step": host.numel() * host.element_size(), "d2h_bytes_per_step": 4,
+                    "api": "underhfs_b200.parallel.zero3.Zero3LM.train_step", "timer": "host wall clock, max over ranks"},
+            "gpu_launches": launches_per_step * args.steps, "final_loss": final_loss,
+        }), flush=True)
+    z.close()
+    if n > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -214,6 +320,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="125m-ddp",
+                    help="125m-ddp is the headline run; the sharded configurations are measured the same way")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

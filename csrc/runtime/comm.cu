@@ -15,6 +15,9 @@
 //                      weights, pushed straight into every peer's parameter
 //                      buffer.  One kernel, no intermediate buffers.
 //   * allgather        gather of equal shards (any dtype) into every rank's buffer.
+//   * gather_segments / rs_adamw_segments: ZeRO-3 per-unit row-sharded
+//                      parameter all-gather (push) and gradient
+//                      reduce-scatter fused with AdamW on the owned rows.
 //   * allreduce (bf16) and reduce_scatter (fp32 / bf16): the same peer-load /
 //                      peer-store scheme for bf16 buffers (fp32 accumulation)
 //                      and for a sharded result.
@@ -26,6 +29,7 @@
 // peer memory are plain ld.global.cg (no TMA, no multicast).
 #include <pybind11/pybind11.h>
 
+#include <array>
 #include <cstring>
 #include <mutex>
 #include <stdexcept>
@@ -317,6 +321,144 @@ __global__ void __launch_bounds__(512) rs_adamw_ag_kernel(const RsAdamArgs a) {
   commit_epoch(a.grads, a.rank, e);
 }
 
+// ----------------------------------------------------------------- ZeRO-3
+// A unit (one transformer block, the embeddings, or the tail) is gathered and
+// reduced as a list of segments: rank r owns rows [r*N/W, (r+1)*N/W) of every
+// parameter matrix of the unit (vectors count as N x 1), stored contiguously
+// in its shard; `nat` is where the segment lives in the unit's natural
+// (gathered, full) layout.  All offsets and lengths are in elements.
+constexpr int kMaxSeg = 16;
+struct SegTable {
+  int n;
+  long long nat[kMaxSeg];
+  long long shard[kMaxSeg];
+  long long len[kMaxSeg];
+};
+
+struct GatherSegArgs {
+  PeerPtrs pp;                  // bf16 gather buffers (symmetric)
+  long long dst_off_bytes;      // unit base inside every rank's gather region
+  const uint4* shard;           // this rank's bf16 shard (16-byte vectors)
+  SegTable t;
+  int rank, world;
+  DeviceStatus* status;
+};
+
+// Push all-gather of one unit: this rank stores its segments into every
+// rank's gather buffer (its own included).  The opening barrier keeps a rank
+// from overwriting a ring slot that a peer is still computing with; the
+// closing one publishes the gathered unit to the next launch.
+__global__ void __launch_bounds__(kCommThreads) gather_segments_kernel(const GatherSegArgs a) {
+  const uint32_t e = next_epoch(a.pp, a.rank);
+  if (!block_barrier(a.pp, a.rank, a.world, kInOff, e, a.status, 150)) {
+    commit_epoch(a.pp, a.rank, e);
+    return;
+  }
+  const long long G = (long long)gridDim.x * blockDim.x;
+  for (int sgi = 0; sgi < a.t.n; ++sgi) {
+    const long long len16 = a.t.len[sgi] / 8;
+    const uint4* src = a.shard + a.t.shard[sgi] / 8;
+    const long long dst = a.dst_off_bytes + a.t.nat[sgi] * 2;
+    for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < len16; base += kUnroll * G) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * G < len16) v[u] = __ldg(src + base + u * G);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (base + u * G >= len16) break;
+#pragma unroll
+        for (int p = 0; p < kMaxWorld; ++p)
+          if (p < a.world) __stcg(reinterpret_cast<uint4*>(a.pp.data[p] + dst) + base + u * G, v[u]);
+      }
+    }
+  }
+  block_barrier(a.pp, a.rank, a.world, kOutOff, e, a.status, 151);
+  commit_epoch(a.pp, a.rank, e);
+}
+
+struct RsSegArgs {
+  PeerPtrs grads;               // fp32 unit gradients in natural layout (symmetric)
+  long long g_off_bytes;
+  SegTable t;
+  float* master;                // this rank's shard: fp32 master / moments, bf16 copy
+  float* m;
+  float* v;
+  __nv_bfloat16* shard16;
+  float lr, beta1, beta2, eps, weight_decay, grad_scale;
+  int decoupled;
+  const int* step_ptr;
+  int rank, world;
+  DeviceStatus* status;
+};
+
+// Reduce-scatter of one unit's gradients fused with AdamW on the owned rows:
+// sum this rank's segments over every peer's gradient buffer (peer loads),
+// update fp32 master / moments and the bf16 shard in place.  The closing
+// barrier tells every rank its gradient buffer has been read.
+__global__ void __launch_bounds__(kCommThreads) rs_adamw_segments_kernel(const RsSegArgs a) {
+  const uint32_t e = next_epoch(a.grads, a.rank);
+  if (!block_barrier(a.grads, a.rank, a.world, kInOff, e, a.status, 160)) {
+    commit_epoch(a.grads, a.rank, e);
+    return;
+  }
+  const int step = *a.step_ptr;
+  const float bc1 = 1.0f - powf(a.beta1, (float)step);
+  const float bc2 = 1.0f - powf(a.beta2, (float)step);
+  const float step_size = a.lr / bc1;
+  const float inv_sqrt_bc2 = rsqrtf(bc2);
+  const long long G = (long long)gridDim.x * blockDim.x;
+  for (int sgi = 0; sgi < a.t.n; ++sgi) {
+    const long long len4 = a.t.len[sgi] / 4;
+    const long long g4 = a.t.nat[sgi] / 4;
+    const long long s4 = a.t.shard[sgi] / 4;
+    for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < len4; base += kUnroll * G) {
+      float4 gv[kUnroll][kMaxWorld];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int p = 0; p < kMaxWorld; ++p)
+          if (p < a.world && base + u * G < len4)
+            gv[u][p] = __ldcg(reinterpret_cast<const float4*>(a.grads.data[p] + a.g_off_bytes) + g4 + base + u * G);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const long long i = base + u * G;
+        if (i >= len4) break;
+        float gr[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < kMaxWorld; ++p)
+          if (p < a.world) {
+            gr[0] += gv[u][p].x;
+            gr[1] += gv[u][p].y;
+            gr[2] += gv[u][p].z;
+            gr[3] += gv[u][p].w;
+          }
+        float4 p4 = reinterpret_cast<float4*>(a.master)[s4 + i];
+        float4 m4 = reinterpret_cast<float4*>(a.m)[s4 + i];
+        float4 v4 = reinterpret_cast<float4*>(a.v)[s4 + i];
+        float pw[4] = {p4.x, p4.y, p4.z, p4.w};
+        float mw[4] = {m4.x, m4.y, m4.z, m4.w};
+        float vw[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float gg = gr[j] * a.grad_scale;
+          if (a.decoupled) pw[j] -= a.lr * a.weight_decay * pw[j];
+          else gg += a.weight_decay * pw[j];
+          mw[j] = a.beta1 * mw[j] + (1.0f - a.beta1) * gg;
+          vw[j] = a.beta2 * vw[j] + (1.0f - a.beta2) * gg * gg;
+          pw[j] -= step_size * mw[j] / (sqrtf(vw[j]) * inv_sqrt_bc2 + a.eps);
+        }
+        reinterpret_cast<float4*>(a.master)[s4 + i] = make_float4(pw[0], pw[1], pw[2], pw[3]);
+        reinterpret_cast<float4*>(a.m)[s4 + i] = make_float4(mw[0], mw[1], mw[2], mw[3]);
+        reinterpret_cast<float4*>(a.v)[s4 + i] = make_float4(vw[0], vw[1], vw[2], vw[3]);
+        reinterpret_cast<uint2*>(a.shard16)[s4 + i] = make_uint2(pack_bf16x2(pw[0], pw[1]), pack_bf16x2(pw[2], pw[3]));
+      }
+    }
+  }
+  block_barrier(a.grads, a.rank, a.world, kOutOff, e, a.status, 161);
+  commit_epoch(a.grads, a.rank, e);
+}
+
 struct AgArgs {
   PeerPtrs pp;
   long long off_bytes;
@@ -521,6 +663,66 @@ void comm_allgather(const SymmetricHeap& h, long long off_bytes, long long shard
   a.world = h.world();
   a.status = device_status_ptr();
   allgather_kernel<<<clamp_blocks(blocks), 512, 0, s>>>(a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+static SegTable seg_table(const std::vector<std::array<long long, 3>>& segs, int align) {
+  if (segs.size() > (size_t)kMaxSeg) throw std::invalid_argument("too many segments in one unit");
+  SegTable t{};
+  t.n = (int)segs.size();
+  for (size_t i = 0; i < segs.size(); ++i) {
+    t.nat[i] = segs[i][0];
+    t.shard[i] = segs[i][1];
+    t.len[i] = segs[i][2];
+    if (t.nat[i] % align || t.shard[i] % align || t.len[i] % align)
+      throw std::invalid_argument("segment offsets and lengths must be multiples of 8 elements");
+  }
+  return t;
+}
+
+void comm_gather_segments(const SymmetricHeap& h, long long dst_off_bytes, uintptr_t shard,
+                          const std::vector<std::array<long long, 3>>& segs, int blocks, cudaStream_t s) {
+  if (dst_off_bytes % 16 != 0 || shard % 16 != 0) throw std::invalid_argument("gather needs 16-byte alignment");
+  GatherSegArgs a{};
+  a.pp = peer_ptrs(h);
+  a.dst_off_bytes = dst_off_bytes;
+  a.shard = reinterpret_cast<const uint4*>(shard);
+  a.t = seg_table(segs, 8);
+  a.rank = h.rank();
+  a.world = h.world();
+  a.status = device_status_ptr();
+  gather_segments_kernel<<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+void comm_rs_adamw_segments(const SymmetricHeap& grads, long long g_off_bytes,
+                            const std::vector<std::array<long long, 3>>& segs, uintptr_t master, uintptr_t m,
+                            uintptr_t v, uintptr_t shard16, float lr, float beta1, float beta2, float eps,
+                            float weight_decay, float grad_scale, bool decoupled, uintptr_t step_ptr, int blocks,
+                            cudaStream_t s) {
+  if (g_off_bytes % 16 != 0) throw std::invalid_argument("gradient unit must be 16-byte aligned");
+  RsSegArgs a{};
+  a.grads = peer_ptrs(grads);
+  a.g_off_bytes = g_off_bytes;
+  a.t = seg_table(segs, 8);
+  a.master = reinterpret_cast<float*>(master);
+  a.m = reinterpret_cast<float*>(m);
+  a.v = reinterpret_cast<float*>(v);
+  a.shard16 = reinterpret_cast<__nv_bfloat16*>(shard16);
+  a.lr = lr;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.eps = eps;
+  a.weight_decay = weight_decay;
+  a.grad_scale = grad_scale;
+  a.decoupled = decoupled ? 1 : 0;
+  a.step_ptr = reinterpret_cast<const int*>(step_ptr);
+  a.rank = grads.rank();
+  a.world = grads.world();
+  a.status = device_status_ptr();
+  rs_adamw_segments_kernel<<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

@@ -1,6 +1,9 @@
 // Host interface of the symmetric heap and fused collectives (comm.cu).
 #pragma once
 
+#include <array>
+#include <vector>
+
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -48,6 +51,13 @@ void comm_allreduce_bf16(const SymmetricHeap& h, long long off_bytes, long long 
                          cudaStream_t s);
 void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long long out_off_bytes, long long n,
                          bool bf16, float scale, int blocks, cudaStream_t s);
+void comm_gather_segments(const SymmetricHeap& h, long long dst_off_bytes, uintptr_t shard,
+                          const std::vector<std::array<long long, 3>>& segs, int blocks, cudaStream_t s);
+void comm_rs_adamw_segments(const SymmetricHeap& grads, long long g_off_bytes,
+                            const std::vector<std::array<long long, 3>>& segs, uintptr_t master, uintptr_t m,
+                            uintptr_t v, uintptr_t shard16, float lr, float beta1, float beta2, float eps,
+                            float weight_decay, float grad_scale, bool decoupled, uintptr_t step_ptr, int blocks,
+                            cudaStream_t s);
 void comm_barrier(const SymmetricHeap& h, cudaStream_t s);
 void comm_wait_probe(const SymmetricHeap& h, unsigned int want, unsigned long long bound_ns, cudaStream_t s);
 

@@ -116,6 +116,17 @@ void bind_comm(py::module_& m) {
                                   float scale, int blocks, uintptr_t s) {
     comm_reduce_scatter(h, in_off, out_off, n, bf16, scale, blocks, S(s));
   });
+  m.def("comm_gather_segments", [](const SymmetricHeap& h, long long dst_off, uintptr_t shard,
+                                   const std::vector<std::array<long long, 3>>& segs, int blocks, uintptr_t s) {
+    comm_gather_segments(h, dst_off, shard, segs, blocks, S(s));
+  });
+  m.def("comm_rs_adamw_segments",
+        [](const SymmetricHeap& g, long long goff, const std::vector<std::array<long long, 3>>& segs, uintptr_t master,
+           uintptr_t mm, uintptr_t vv, uintptr_t shard16, float lr, float b1, float b2, float eps, float wd,
+           float gscale, bool decoupled, uintptr_t step_ptr, int blocks, uintptr_t s) {
+          comm_rs_adamw_segments(g, goff, segs, master, mm, vv, shard16, lr, b1, b2, eps, wd, gscale, decoupled,
+                                 step_ptr, blocks, S(s));
+        });
   m.def("comm_barrier", [](const SymmetricHeap& h, uintptr_t s) { comm_barrier(h, S(s)); });
   m.def("comm_wait_probe", [](const SymmetricHeap& h, unsigned int want, unsigned long long bound_ns, uintptr_t s) {
     comm_wait_probe(h, want, bound_ns, S(s));

@@ -129,11 +129,53 @@ def case_zero(rank: int, world: int) -> None:
     assert all(torch.equal(allp[0], q) for q in allp)
 
 
+def case_zero3(rank: int, world: int) -> None:
+    """ZeRO-3 (sharded weights, per-unit gather, RS fused with AdamW) against a
+    replicated model with FusedAdamW on all-reduced gradients."""
+    from underhfs_b200.nn import TransformerLM
+    from underhfs_b200.optim import FusedAdamW
+    from underhfs_b200.parallel.zero3 import Zero3LM
+
+    kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
+    for tied in (True, False):
+        cpu = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=3, heads=4,
+                            tied=tied, init="normal", seed=3)
+        state = {n: p._data.detach().float().clone() for n, p in cpu.named_parameters()}
+        ref = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=3, heads=4,
+                            tied=tied, init="normal", seed=3)
+        ref.to(f"cuda:{torch.cuda.current_device()}", dtype="bf16")
+        ref_opt = FusedAdamW(ref.parameters(), **kw)
+        z = Zero3LM(cpu.spec, rank=rank, world=world, state=state, blocks=16, **kw)
+        gen = torch.Generator().manual_seed(300 + rank)
+        for _ in range(3):
+            ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+            tg = torch.roll(ids, -1, 1)
+            ref.zero_grad()
+            ref(ids, tg).backward()
+            dist.all_reduce(ref.flat.grads)
+            ref.flat.grads /= world
+            ref_opt.step()
+            loss = z.train_step(ids, tg)
+        torch.cuda.synchronize()
+        from underhfs_b200.ops._lib import core
+
+        st = core().device_status(True)
+        assert st["code"] == 0, st
+        assert torch.isfinite(loss).item()
+        full = z.full_state()
+        for name, slot in ref.flat.by_name.items():
+            a = full[name].reshape(-1)
+            b = ref.flat.master[slot.offset: slot.offset + slot.numel].float().cpu()
+            err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+            assert err < 2e-2, (tied, name, err)
+        z.close()
+
+
 def main() -> int:
     case = sys.argv[1]
     rank, world = _setup()
     try:
-        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero}[case](rank, world)
+        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3}[case](rank, world)
         dist.barrier()
         if rank == 0:
             print(f"OK {case}", flush=True)

@@ -14,6 +14,15 @@ import pytest
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
+
+def _gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
 ROOT = Path(__file__).resolve().parents[1]
 
 
@@ -23,8 +32,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero"])
+@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero", "zero3"])
 def test_two_gpu_case(case):
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
     env = dict(os.environ)
     env["PYTHONPATH"] = str(ROOT) + os.pathsep + env.get("PYTHONPATH", "")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",

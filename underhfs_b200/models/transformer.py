@@ -209,6 +209,18 @@ class LMEngine:
         self.tail_range = (flat.by_name["norm.weight"].offset, flat.numel)
         self.embed_range = (0, self.blocks[0]["range"][0] if self.blocks else flat.by_name["norm.weight"].offset)
 
+    # Unit hooks: a unit is "embed", a block index, or "tail".  Sharded-parameter
+    # engines (ZeRO-3) gather a unit's weights before it runs and reduce its
+    # gradients after its backward; the flat-buffer engine needs neither.
+    def unit_forward(self, unit) -> None:
+        pass
+
+    def unit_backward_begin(self, unit) -> None:
+        pass
+
+    def unit_backward_end(self, unit) -> None:
+        pass
+
     # ------------------------------------------------------------ forward
     def forward(self, ids: torch.Tensor, targets: torch.Tensor | None, *, fuse_loss_grad: bool,
                 keep_logits: bool = False):
@@ -220,9 +232,11 @@ class LMEngine:
         M = B * T
         H, D = s.heads, s.head_dim
         ids = ids.reshape(-1)
+        self.unit_forward("embed")
         x = K.embedding(ids, self.E, self.P, T)
         saved_blocks = []
-        for blk in self.blocks:
+        for bi, blk in enumerate(self.blocks):
+            self.unit_forward(bi)
             h1, r1 = K.rmsnorm(x, blk["ln1"], s.eps)
             qkv = K.linear_fwd(h1, blk["Wqkv"], blk["bqkv"])
             o, lse = K.flash_attn_qkv(qkv, B, T, H, D, self.causal)
@@ -232,6 +246,7 @@ class LMEngine:
             x2 = K.linear_fwd_resid(g, blk["W2"], blk["b2"], x1)
             saved_blocks.append((x, h1, r1, qkv, o, lse, x1, h2, r2, u, g))
             x = x2
+        self.unit_forward("tail")
         hf, rf = K.rmsnorm(x, self.lnf, s.eps)
         logits = K.linear_fwd(hf, self.Wh, None)
         loss = None
@@ -280,15 +295,19 @@ class LMEngine:
             # (p - onehot) / M * dL/dloss, computed in place over the kept logits
             K.softmax_cross_entropy(dl, sv["targets"], dl, 1.0 / M, loss_grad)
         # head + final norm
+        self.unit_backward_begin("tail")
         dhf = K.linear_dgrad(dl, self.Wh)
         K.linear_wgrad_accum(dl, sv["hf"], self.gWh)
         dx = K.rmsnorm_backward(dhf, sv["xL"], self.lnf, sv["rf"], None, self.g_lnf)
+        self.unit_backward_end("tail")
         if hook is not None and not s.tied:
             hook(*self.tail_range)
         elif hook is not None:
             hook(self.flat.by_name["norm.weight"].offset, self.flat.numel)
         del dl, dhf
-        for blk, saved in zip(reversed(self.blocks), reversed(sv["blocks"])):
+        for bi in range(len(self.blocks) - 1, -1, -1):
+            blk, saved = self.blocks[bi], sv["blocks"][bi]
+            self.unit_backward_begin(bi)
             x, h1, r1, qkv, o, lse, x1, h2, r2, u, g = saved
             # MLP
             du = K.linear_dgrad(dx, blk["W2"], gelu_in=u)
@@ -316,9 +335,12 @@ class LMEngine:
             del dqkv
             dx = K.rmsnorm_backward(dh1, x, blk["ln1"], r1, dx1, blk["g_ln1"])
             del dh1, dx1
+            self.unit_backward_end(bi)
             if hook is not None:
                 hook(*blk["range"])
+        self.unit_backward_begin("embed")
         K.embedding_backward(sv["ids"], dx, self.gE, self.gP, T)
+        self.unit_backward_end("embed")
         if hook is not None:
             hook(*self.embed_range)
         self._saved = None
