@@ -6,6 +6,8 @@
 // the sm_100a kernels; these take raw device pointers (Python ints from
 // torch.Tensor.data_ptr()) and a CUDA stream handle, so the Python layer owns
 // memory and streams while every hot op runs a kernel from this library.
+#include <array>
+
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
@@ -167,6 +169,58 @@ PYBIND11_MODULE(_core, m) {
       py::arg("ldb"), py::arg("b_mn"), py::arg("C"), py::arg("ldc"), py::arg("epi"), py::arg("bias") = 0,
       py::arg("aux") = 0, py::arg("ld_aux") = 0, py::arg("aux_out") = 0, py::arg("ld_aux_out") = 0,
       py::arg("splits") = 1, py::arg("block_n") = 0, py::arg("stream") = 0);
+  // GEMM whose B rows are gathered by the kernel itself (ZeRO-3): `segs` are
+  // (src, dst_off_bytes, rows, row_bytes, flag_base) rows this rank pushes.
+  m.def(
+      "gemm_ag",
+      [](int M, int N, int K, uintptr_t A, long long lda, bool a_mn, uintptr_t B, long long ldb, bool b_mn,
+         uintptr_t C, long long ldc, int epi, uintptr_t bias, uintptr_t aux, long long ld_aux, uintptr_t aux_out,
+         long long ld_aux_out, int splits, int world, int rank, unsigned epoch, std::vector<uintptr_t> peer_data,
+         std::vector<uintptr_t> peer_flags, std::vector<std::array<long long, 5>> segs, int b_flag_base,
+         int ready_base, uintptr_t stream) {
+        GemmProblem p;
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.A = P<const __nv_bfloat16>(A);
+        p.lda = lda;
+        p.a_mn = a_mn;
+        p.B = P<const __nv_bfloat16>(B);
+        p.ldb = ldb;
+        p.b_mn = b_mn;
+        p.C = P<void>(C);
+        p.ldc = ldc;
+        p.epi = epi;
+        p.bias = P<const __nv_bfloat16>(bias);
+        p.aux = P<const __nv_bfloat16>(aux);
+        p.ld_aux = ld_aux;
+        p.aux_out = P<__nv_bfloat16>(aux_out);
+        p.ld_aux_out = ld_aux_out;
+        p.splits = splits;
+        if (world < 1 || world > 8 || (int)peer_data.size() != world || (int)peer_flags.size() != world ||
+            segs.size() > 8)
+          throw std::invalid_argument("gemm_ag: bad gather description");
+        p.ag.world = world;
+        p.ag.rank = rank;
+        p.ag.epoch = epoch;
+        for (int r = 0; r < world; ++r) {
+          p.ag.peer_data[r] = reinterpret_cast<char*>(peer_data[r]);
+          p.ag.peer_flags[r] = reinterpret_cast<unsigned*>(peer_flags[r]);
+        }
+        p.ag.nseg = (int)segs.size();
+        for (size_t i = 0; i < segs.size(); ++i) {
+          if (segs[i][0] % 16 || segs[i][1] % 16 || segs[i][3] % 16)
+            throw std::invalid_argument("gemm_ag: gathered rows must be 16-byte aligned");
+          p.ag.seg[i].src = reinterpret_cast<const void*>(segs[i][0]);
+          p.ag.seg[i].dst_off_bytes = segs[i][1];
+          p.ag.seg[i].rows = segs[i][2];
+          p.ag.seg[i].row_bytes = segs[i][3];
+          p.ag.seg[i].flag_base = (int)segs[i][4];
+        }
+        p.ag.b_flag_base = b_flag_base;
+        p.ag.ready_base = ready_base;
+        gemm_bf16_tcgen05(p, S(stream));
+      });
   m.def("gemm_f32", [](uintptr_t A, uintptr_t B, uintptr_t C, int M, int N, int K, bool b_trans, uintptr_t s) {
     gemm_f32_simt(P<const float>(A), P<const float>(B), P<float>(C), M, N, K, b_trans, S(s));
   });

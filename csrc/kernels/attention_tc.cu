@@ -8,9 +8,9 @@
 //   warp 8      TMA producer: Q_A, Q_B once; then K_0, V_0, K_1, V_1, ...
 //               through a ring of 128 x D slots (128B-swizzled, no multicast)
 //   warp 9      TMEM allocator + MMA issuer (one elected thread), ordering
-//                 S_A(j) | PV_B(j-1) | S_B(j) | PV_A(j)
-//               so the tensor core works on one tile while the softmax
-//               warpgroup of the other tile runs:
+//                 S_A(j) | S_B(j) | PV_A(j-1) | PV_B(j-1)
+//               so the next S is computed while the softmax warpgroups still
+//               work on the current block:
 //                 S_t(j)  = Q_t K_j^T   (M=128, N=128, K=D)   -> TMEM S_t
 //                 O_t    += P_t(j) V_j  (M=128, N=D,   K=128) -> TMEM O_t
 //   softmax     thread r of a softmax warpgroup owns query row r of its
@@ -216,33 +216,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       bool ok = mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 210);
+      // S of block j for both tiles goes ahead of PV of block j-1: a softmax
+      // warpgroup frees S as soon as it holds the row in registers, so the
+      // next S is ready when it finishes P, and the PV product overlaps the
+      // next block's exponentials instead of sitting on the critical path.
       for (int j = 0; j < nB && ok; ++j) {
         if (!mbar_wait_bounded(&slot_full[slot_of(2 * j)], phase_of(2 * j), a.status, kErrWaitTimeoutFull, 214)) {
           ok = false;
           break;
         }
-        if (j < nA && !issue_s(0, j)) {
+        if ((j < nA && !issue_s(0, j)) || !issue_s(1, j)) {
           ok = false;
           break;
         }
+        tc_commit(&slot_empty[slot_of(2 * j)]);  // K_j read by both tiles
         if (j >= 1) {
-          if (!issue_pv(1, j - 1)) {
+          if ((j - 1 < nA && !issue_pv(0, j - 1)) || !issue_pv(1, j - 1)) {
             ok = false;
             break;
           }
           tc_commit(&slot_empty[slot_of(2 * (j - 1) + 1)]);  // V_{j-1} read by both tiles
         }
-        if (!issue_s(1, j)) {
-          ok = false;
-          break;
-        }
-        tc_commit(&slot_empty[slot_of(2 * j)]);  // K_j read by both tiles
-        if (j < nA && !issue_pv(0, j)) {
-          ok = false;
-          break;
-        }
       }
-      if (ok && nB > 0 && issue_pv(1, nB - 1)) tc_commit(&slot_empty[slot_of(2 * (nB - 1) + 1)]);
+      if (ok && nB > 0) {
+        if ((nB - 1 < nA && !issue_pv(0, nB - 1)) || !issue_pv(1, nB - 1)) ok = false;
+        else tc_commit(&slot_empty[slot_of(2 * (nB - 1) + 1)]);
+      }
       tc_commit(done);
       mbar_wait_bounded(done, 0, a.status, kErrWaitTimeoutAccum, 215);
     }

@@ -71,6 +71,9 @@ struct BwdCfg {
   static constexpr int kSmem = 1024 + 2 * kTile + kStages * kStageBytes + 2 * kPT + kStages * kVec + 2 * kStage + 128;
   static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + D;
   static constexpr uint32_t kDQ = (D == 64) ? 256 + 2 * D : 0;  // D=128: reuse S^T columns
+  // D=64: two dQ buffers (columns 384 and 448), so dQ of block t is read out
+  // while block t+1's softmax runs; D=128 has no room and reads it in place.
+  static constexpr int kDQBufs = (D == 64) ? 2 : 1;
   static constexpr uint32_t kCols = 512;
 };
 
@@ -109,11 +112,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = bars + 5;       // S^T and dP^T ready
   uint64_t* s_free = bars + 6;       // S^T / dP^T held in registers by all compute threads
   uint64_t* p_full = bars + 7;       // P^T / dS^T written
-  uint64_t* dq_full = bars + 8;      // dQ_i ready (dQ MMAs of step i done)
-  uint64_t* dq_free = bars + 9;      // dQ_i read
-  uint64_t* pt_free = bars + 10;     // dV / dK MMAs of step i done: P^T / dS^T reusable
-  uint64_t* done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  // one dQ ready / read barrier pair per dQ buffer, so that neither side can
+  // get two phases ahead of the other
+  uint64_t* dq_full = bars + 8;      // [2] dQ of a step ready (dQ MMAs done)
+  uint64_t* dq_free = bars + 10;     // [2] dQ of a step read out
+  uint64_t* pt_free = bars + 12;     // dV / dK MMAs of step i done: P^T / dS^T reusable
+  uint64_t* done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -139,8 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(s_full, 1);
     mbar_init(s_free, kCompute);
     mbar_init(p_full, kCompute);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, kCompute);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], kCompute);
+    }
     mbar_init(pt_free, 1);
     mbar_init(done, 1);
     fence_barrier_init();
@@ -251,9 +258,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint32_t off = (kk * 16 * 128) >> 4;
-          tc_mma_f16(tmem + Cfg::kDQ, mnmaj + dst16 + off, mnmaj + k16 + off, id_q, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tmem + Cfg::kDQ + (uint32_t)((t % Cfg::kDQBufs) * D), mnmaj + dst16 + off, mnmaj + k16 + off,
+                     id_q, kk > 0 ? 1u : 0u);
         }
-        tc_commit(dq_full);
+        tc_commit(&dq_full[t % Cfg::kDQBufs]);
         // dV += P^T dO ; dK += dS^T Q    (K = 128 queries: sub-tile kk>>2 of the P^T / dS^T tiles)
 #pragma unroll 1
         for (int kk = 0; kk < BQ / 16; ++kk) {
@@ -279,7 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (!mbar_wait_bounded(p_full, (uint32_t)t & 1u, a.status, kErrWaitTimeoutAccum, 314) ||
-              (t > 0 && !mbar_wait_bounded(dq_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 315))) {
+              (t >= Cfg::kDQBufs &&
+               !mbar_wait_bounded(&dq_free[t % Cfg::kDQBufs], (uint32_t)(t / Cfg::kDQBufs - 1) & 1u, a.status,
+                                  kErrWaitTimeoutAccum, 315))) {
             ok = false;
             break;
           }
@@ -290,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dQ shares the S^T columns: strictly one block after the other
         for (int t = 0; t < steps && ok; ++t) {
           if (t > 0 && (!mbar_wait_bounded(s_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 312) ||
-                        !mbar_wait_bounded(dq_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 313))) {
+                        !mbar_wait_bounded(&dq_free[0], (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 313))) {
             ok = false;
             break;
           }
@@ -322,6 +332,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     // runs the same sequence of named barriers for every step; after a failed
     // wait a thread only skips the work.
     bool ok = true;
+    // dQ of block tt: TMEM -> registers -> swizzled fp32 box -> TMA
+    // reduce-add into the fp32 accumulator.  Rows past T add zeros (P is 0).
+    auto readout = [&](int tt) {
+      const int q0 = (i_start + tt) * BQ;
+      const int bi = tt % Cfg::kDQBufs;
+      const uint32_t buf = (uint32_t)(bi * D);
+      if (ok && !mbar_wait_warp(&dq_full[bi], (uint32_t)(tt / Cfg::kDQBufs) & 1u, a.status, kErrWaitTimeoutAccum, 322))
+        ok = false;
+#pragma unroll 1
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t v[32];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + buf + half * (D / 2) + c * 32, v);
+          tmem_wait_ld_regs<32>(v);
+          if (c == D / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(&dq_free[bi]);  // this dQ buffer may be overwritten
+          }
+        }
+        if (leader) bulk_wait_group_read0();  // the previous reduction has read the box
+        named_barrier_sync(1 + half, 128);
+        if (ok) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
+          fence_proxy_async_smem();
+        }
+        named_barrier_sync(1 + half, 128);
+        if (leader && ok) {
+          tma_reduce_add_2d(&tm_dq, stage, h * D + half * (D / 2) + c * 32, row0 + q0);
+          bulk_commit_group();
+        }
+      }
+    };
     for (int t = 0; t < steps; ++t) {
       const int st = t % S;
       const uint32_t tp = t & 1;
@@ -378,39 +424,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async_smem();
           mbar_arrive(p_full);
-          if (!mbar_wait_warp(dq_full, tp, a.status, kErrWaitTimeoutAccum, 322)) ok = false;
         }
       }
-      // dQ_i: TMEM -> registers -> swizzled fp32 box -> TMA reduce-add into
-      // the fp32 accumulator.  Rows past T add zeros (P is 0 there).
-#pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t v[32];
-        if (ok) {
-          tc_fence_after();
-          tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + half * (D / 2) + c * 32, v);
-          tmem_wait_ld_regs<32>(v);
-          if (c == D / 64 - 1) {
-            tc_fence_before();
-            mbar_arrive(dq_free);  // TMEM dQ may be overwritten
-          }
-        }
-        if (leader) bulk_wait_group_read0();  // the previous reduction has read the box
-        named_barrier_sync(1 + half, 128);
-        if (ok) {
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                make_uint4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
-          fence_proxy_async_smem();
-        }
-        named_barrier_sync(1 + half, 128);
-        if (leader && ok) {
-          tma_reduce_add_2d(&tm_dq, stage, h * D + half * (D / 2) + c * 32, row0 + q0);
-          bulk_commit_group();
-        }
-      }
+      // one dQ buffer: read it now; two: read the previous block's while this
+      // block's dQ product runs
+      if (Cfg::kDQBufs == 1) readout(t);
+      else if (t > 0) readout(t - 1);
     }
+    if (Cfg::kDQBufs == 2 && steps > 0) readout(steps - 1);
     if (leader) bulk_wait_group0();
     // the last dV / dK products have retired
     if (ok && steps > 0 &&

@@ -16,6 +16,35 @@ enum GemmEpilogue : int {
   GEMM_EPI_F32_STORE = 5,  // C = acc    (fp32)
 };
 
+// Fused all-gather of B rows (ZeRO-3 weights).  The kernel's pusher warp
+// copies this rank's rows of a unit's weight matrices into every rank's
+// gather buffer and publishes one flag per 32 rows (release, system scope);
+// the TMA producer waits for the flags covering a B tile (K-major B: the
+// tile's N rows; MN-major B: the k-block's rows) before loading it from the
+// local gather buffer.  Flags hold an epoch that grows with every gather, so
+// they are never reset.  Before pushing into rank p a pusher waits for p's
+// ready flag: p raises it when this kernel starts there, i.e. after p has
+// finished every earlier kernel that read the same gather slot.
+struct GemmGatherSeg {
+  const void* src = nullptr;    // this rank's rows (local shard), row-contiguous
+  long long dst_off_bytes = 0;  // where these rows go inside every rank's gather region
+  long long rows = 0;
+  long long row_bytes = 0;      // multiple of 16
+  int flag_base = 0;            // flag index of the first 32-row chunk
+};
+
+struct GemmGather {
+  int world = 0;  // 0 = no fused gather
+  int rank = 0;
+  unsigned epoch = 0;
+  char* peer_data[8] = {};      // gather region base on every rank
+  unsigned* peer_flags[8] = {};  // flag array on every rank
+  int nseg = 0;                 // segments this kernel pushes (0 = only wait)
+  GemmGatherSeg seg[8];
+  int b_flag_base = -1;         // flag of B row 0; -1 = B is not gathered
+  int ready_base = 0;           // per-rank ready flags start here
+};
+
 struct GemmProblem {
   int M = 0, N = 0, K = 0;
   const __nv_bfloat16* A = nullptr;  // K-major: A[m*lda + k]; MN-major: A[k*lda + m]
@@ -36,6 +65,7 @@ struct GemmProblem {
                       // ranges per CTA, partial tiles accumulated by the fp32 epilogue)
   int block_n = 0;    // 0 = choose, else 128 or 256
   int max_ctas = 0;   // 0 = one per SM
+  GemmGather ag;      // fused all-gather of B rows (ZeRO-3), off by default
 };
 
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream);

@@ -13,14 +13,17 @@
 // Replaces the reference's cublasSgemm call in CudaTensorF32::matmul
 // (cuda/kernels.cu:488-493) and its Python matmul (tensor.py:609-675).
 //
-// CTA layout (320 threads, one CTA per SM, persistent over tiles):
+// CTA layout (352 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer (one elected lane), 128B-swizzled tiles, no
 //               multicast (this kernel also runs inside multi-GPU jobs)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane)
 //   warps 2..9  epilogue: tcgen05.ld 32 lanes each (warp % 4 selects the
 //               lane quarter, (warp - 2) / 4 the half of the BN columns),
 //               fused bias / GELU / residual / dGELU / fp32-accumulate,
-//               vectorized stores
+//               TMA-store epilogue
+//   warp 10     pusher of the fused all-gather (ZeRO-3 weights): copies this
+//               rank's rows to every peer over NVLink (peer stores) while
+//               the other warps compute; idle without a gather
 // The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of
 // tile i overlaps the main loop of tile i+1.  Every wait is bounded.
 #include <cudaTypedefs.h>
@@ -39,7 +42,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;           // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 320;   // producer, MMA, 8 epilogue warps
+constexpr int kThreads = 352;   // producer, MMA, 8 epilogue warps, pusher (fused all-gather)
 constexpr int kSmemBudget = 200 * 1024;
 
 template <int BN>
@@ -73,7 +76,42 @@ struct GemmArgs {
   __nv_bfloat16* aux_out;
   long long ld_aux_out;
   DeviceStatus* status;
+  GemmGather ag;
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until a flag reaches `epoch` (wrap-safe comparison).
+__device__ __forceinline__ bool wait_epoch(const uint32_t* f, uint32_t epoch, DeviceStatus* st, int where) {
+  if ((int32_t)(ld_acquire_sys_u32(f) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if ((int32_t)(ld_acquire_sys_u32(f) - epoch) >= 0) return true;
+    if (((++spins) & 63u) == 0u && globaltimer_ns() - t0 > kWaitBoundNs) {
+      report_error(st, kErrPeerTimeout, where);
+      return false;
+    }
+  }
+}
+
+// Wait for the gathered B rows [r0, r1) (32-row flags of this rank), then
+// order the remote generic-proxy stores before this thread's TMA loads.
+__device__ __forceinline__ bool wait_gathered_rows(const GemmGather& g, int r0, int r1, DeviceStatus* st) {
+  const uint32_t* flags = g.peer_flags[g.rank] + g.b_flag_base;
+  for (int c = r0 / 32; c < (r1 + 31) / 32; ++c)
+    if (!wait_epoch(flags + c, g.epoch, st, 40)) return false;
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, int& tn, int& split);
 
@@ -229,7 +267,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tm, tn, kb0, kb1;
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * BM, n0 = tn * BN;
+        const bool gathered_b = args.ag.world > 0 && args.ag.b_flag_base >= 0;
+        if (gathered_b && !B_MN && !wait_gathered_rows(args.ag, n0, min(args.N, n0 + BN), args.status)) {
+          ok = false;
+          break;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (gathered_b && B_MN && !wait_gathered_rows(args.ag, kb * BK, min(args.K, kb * BK + BK), args.status)) {
+            ok = false;
+            break;
+          }
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.status, kErrWaitTimeoutEmpty, 10)) {
             ok = false;
             break;
@@ -313,6 +360,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       // All MMAs issued by this thread retire before TMEM is released.
       tc_commit(done);
       mbar_wait_bounded(done, 0, args.status, kErrWaitTimeoutAccum, 22);
+    }
+  } else if (warp == kThreads / 32 - 1) {
+    // ------------------------------------------------------------ pusher
+    const GemmGather& g = args.ag;
+    if (g.world > 0) {
+      // this rank is ready to receive this gather (every earlier kernel that
+      // read the slot has finished here): tell every peer
+      if (blockIdx.x == 0 && lane < g.world)
+        st_release_sys_u32(g.peer_flags[lane] + g.ready_base + g.rank, g.epoch);
+      long long total = 0;
+      for (int s2 = 0; s2 < g.nseg; ++s2) total += (g.seg[s2].rows + 31) / 32;
+      uint32_t ready_mask = 0;
+      bool ok = true;
+      for (long long item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        int s2 = 0;
+        long long c = item;
+        while (c >= (g.seg[s2].rows + 31) / 32) {
+          c -= (g.seg[s2].rows + 31) / 32;
+          ++s2;
+        }
+        const GemmGatherSeg& sg = g.seg[s2];
+        const long long r0 = c * 32, nrows = min(32ll, sg.rows - r0);
+        const long long n16 = nrows * sg.row_bytes / 16;
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(sg.src) + r0 * sg.row_bytes);
+        for (int k = 0; k < g.world && ok; ++k) {
+          const int p = (g.rank + 1 + k) % g.world;  // spread the first pushes over the peers
+          if (!(ready_mask & (1u << p))) {
+            int good = 1;
+            if (lane == 0) good = wait_epoch(g.peer_flags[g.rank] + g.ready_base + p, g.epoch, args.status, 41);
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good) {
+              ok = false;
+              break;
+            }
+            ready_mask |= 1u << p;
+          }
+          uint4* dst = reinterpret_cast<uint4*>(g.peer_data[p] + sg.dst_off_bytes + r0 * sg.row_bytes);
+          for (long long i = lane; i < n16; i += 128) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (i + u * 32 < n16) v[u] = __ldg(src + i + u * 32);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (i + u * 32 < n16) __stcg(dst + i + u * 32, v[u]);
+          }
+        }
+        __syncwarp();
+        if (ok && lane < g.world) {
+          __threadfence_system();
+          st_release_sys_u32(g.peer_flags[lane] + sg.flag_base + c, g.epoch);
+        }
+        __syncwarp();
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -529,6 +630,8 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   a.aux_out = p.aux_out;
   a.ld_aux_out = p.ld_aux_out;
   a.status = device_status_ptr();
+  a.ag = p.ag;
+  if (a.ag.world > 8 || a.ag.nseg > 8) throw std::runtime_error("gemm: fused gather supports 8 ranks / 8 segments");
   const long long units = a.stream_k ? (long long)a.tiles_m * a.tiles_n * a.kb_total
                                      : (long long)a.tiles_m * a.tiles_n * a.splits;
   int grid = units < num_sms() ? (int)units : num_sms();

@@ -137,7 +137,7 @@ def case_zero3(rank: int, world: int) -> None:
     from underhfs_b200.parallel.zero3 import Zero3LM
 
     kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
-    for tied in (True, False):
+    for tied, fused in ((True, True), (False, True), (True, False)):
         cpu = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=3, heads=4,
                             tied=tied, init="normal", seed=3)
         state = {n: p._data.detach().float().clone() for n, p in cpu.named_parameters()}
@@ -145,7 +145,8 @@ def case_zero3(rank: int, world: int) -> None:
                             tied=tied, init="normal", seed=3)
         ref.to(f"cuda:{torch.cuda.current_device()}", dtype="bf16")
         ref_opt = FusedAdamW(ref.parameters(), **kw)
-        z = Zero3LM(cpu.spec, rank=rank, world=world, state=state, blocks=16, **kw)
+        z = Zero3LM(cpu.spec, rank=rank, world=world, state=state, blocks=16, fused_gather=fused, **kw)
+        assert z.fused == fused
         gen = torch.Generator().manual_seed(300 + rank)
         for _ in range(3):
             ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
@@ -167,7 +168,7 @@ def case_zero3(rank: int, world: int) -> None:
             a = full[name].reshape(-1)
             b = ref.flat.master[slot.offset: slot.offset + slot.numel].float().cpu()
             err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
-            assert err < 2e-2, (tied, name, err)
+            assert err < 2e-2, (tied, fused, name, err)
         z.close()
 
 

@@ -49,11 +49,33 @@ def gemm_raw(
     splits: int = 1,
     block_n: int = 0,
 ) -> None:
-    """tcgen05 GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k) with a fused epilogue."""
+    """tcgen05 GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k) with a fused epilogue.
+
+    When a B-gather resolver is installed (ZeRO-3 with fused gathers) and B
+    lives in a gather slot, the launch carries the all-gather of B's rows.
+    """
+    ag = _b_gather(b, b_mn) if _b_gather is not None else None
+    if ag is not None:
+        core().gemm_ag(
+            M, N, K, ptr(a), lda, a_mn, ptr(b), ldb, b_mn, ptr(c), ldc, epi, ptr(bias), ptr(aux), ld_aux,
+            ptr(aux_out), ld_aux_out, splits, *ag, stream(),
+        )
+        return
     core().gemm(
         M, N, K, ptr(a), lda, a_mn, ptr(b), ldb, b_mn, ptr(c), ldc, epi, ptr(bias), ptr(aux), ld_aux,
         ptr(aux_out), ld_aux_out, splits, block_n, stream(),
     )
+
+
+# ZeRO-3 hook: callable (b_tensor, b_mn) -> gather arguments for gemm_ag or None
+_b_gather = None
+
+
+def set_b_gather(resolver) -> None:
+    """Install (or clear with None) the resolver that attaches a fused
+    all-gather to GEMMs whose B operand is a gathered weight."""
+    global _b_gather
+    _b_gather = resolver
 
 
 def _splits_for(tiles: int, k: int) -> int:

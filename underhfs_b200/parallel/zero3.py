@@ -130,9 +130,10 @@ class Zero3LM:
                  group=None, init: str = "normal", seed: int = 0, state: dict | None = None,
                  lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, decoupled: bool = True, blocks: int = 128,
-                 overlap: bool = True) -> None:
+                 overlap: bool = True, fused_gather: bool = True) -> None:
         self.spec = spec
         self.overlap = overlap
+        self.fused = fused_gather
         self.rank, self.world = rank, world
         self.device = torch.device(device)
         self.lr, self.betas, self.eps = lr, betas, eps
@@ -155,13 +156,26 @@ class Zero3LM:
         blk = max(self.units[i].size for i in range(spec.layers)) if spec.layers else 0
         self.slot_off = {"embed": 0, "tail": emb, 0: emb + tail, 1: emb + tail + blk}
         total = emb + tail + 2 * blk
-        self.gsym = SymmetricBuffer(total * 2 + 4096, rank=rank, world=world, group=group)
+        # fused gathers: per slot (tail, ring 0, ring 1) one uint32 flag per 32
+        # gathered rows of the unit's matrices, then one ready flag per rank
+        self._plan_fused()
+        self.flag_words = _round_up(self.max_chunks + world, 64)
+        self.flag_off = {k: _round_up(total * 2, 256) + i * self.flag_words * 4
+                         for i, k in enumerate(("tail", 0, 1))}
+        gbytes = _round_up(total * 2, 256) + 3 * self.flag_words * 4
+        self.gsym = SymmetricBuffer(gbytes + 4096, rank=rank, world=world, group=group)
         self.gradsym = SymmetricBuffer(total * 4 + 4096, rank=rank, world=world, group=group)
         self.gather_buf = self.gsym.tensor(total, torch.bfloat16, offset_bytes=0)
         self.grad_buf = self.gradsym.tensor(total, torch.float32, offset_bytes=0)
         self.gather_buf.zero_()
         self.grad_buf.zero_()
+        self.gsym.tensor(3 * self.flag_words, torch.int32, offset_bytes=self.flag_off["tail"]).zero_()
+        self.epoch = {"tail": 0, 0: 0, 1: 0}
+        self.pending: dict = {}
         self._gathered: dict = {}
+        if self.fused:
+            torch.cuda.synchronize(self.device)
+            K.set_b_gather(self._resolve_b)
         self.engine = Zero3Engine(spec, self)
         self.stream = lambda: torch.cuda.current_stream().cuda_stream
 
@@ -224,6 +238,76 @@ class Zero3LM:
                 self.master[soff: soff + ln].copy_(part.to(self.device, torch.float32))
         self.shard16.copy_(self.master)
 
+    # ------------------------------------------------------ fused gather
+    def _is_matrix(self, slot) -> bool:
+        return len(slot.shape) == 2 and slot.shape[1] > 1
+
+    def _plan_fused(self) -> None:
+        """Flag numbering for the matrices of every fused unit (blocks, tail):
+        chunk c of matrix m covers its gathered rows [32c, 32c+32)."""
+        W = self.world
+        self.flag_base: dict = {}
+        self.max_chunks = 0
+        for key, u in self.units.items():
+            if key == "embed":
+                continue
+            n = 0
+            for s in u.slots:
+                if self._is_matrix(s):
+                    if (s.shape[0] // W) % 32 != 0:
+                        self.fused = False  # rows per rank must be whole 32-row chunks
+                    self.flag_base[(key, s.name)] = n
+                    n += s.shape[0] // 32
+            self.max_chunks = max(self.max_chunks, n)
+
+    def _gather_fused(self, key) -> None:
+        """Small parameters now (a barrier-bracketed gather kernel that also
+        marks the unit boundary on every rank); the matrices are pushed by the
+        first GEMM that reads them (gemm_ag)."""
+        slot = self._slot_key(key)
+        u = self.units[key]
+        small = [list(sg) for s, sg in zip(u.slots, u.segs) if not self._is_matrix(s)]
+        if small:
+            core().comm_gather_segments(self.gsym.heap, self.slot_off[slot] * 2, self.shard16.data_ptr(), small,
+                                        self.nblocks, self.stream())
+        self.epoch[slot] += 1
+        self.pending[slot] = key
+        self._gathered[slot] = key
+
+    def _resolve_b(self, b: torch.Tensor, b_mn: bool):
+        """Gather arguments for a GEMM whose B operand lies in a fused slot."""
+        base = self.gather_buf.data_ptr()
+        off = (b.data_ptr() - base) // 2
+        if off < 0 or off >= self.gather_buf.numel():
+            return None
+        for slot in ("tail", 0, 1):
+            lo = self.slot_off[slot]
+            key = self._gathered.get(slot)
+            if key is None or not (lo <= off < lo + self.units[key].size):
+                continue
+            u = self.units[key]
+            nat = off - lo
+            name = next((s.name for s in u.slots if s.offset - u.lo == nat and self._is_matrix(s)), None)
+            if name is None:
+                return None
+            segs = []
+            if self.pending.get(slot) == key:
+                W, r = self.world, self.rank
+                for s, (snat, soff, ln) in zip(u.slots, u.segs):
+                    if not self._is_matrix(s):
+                        continue
+                    rows = s.shape[0] // W
+                    cols = s.numel // s.shape[0]
+                    segs.append([self.shard16.data_ptr() + soff * 2, (lo + snat) * 2, rows, cols * 2,
+                                 self.flag_base[(key, s.name)] + r * rows // 32])
+                self.pending[slot] = None
+            heap = self.gsym.heap
+            data = [heap.data_ptr(p) for p in range(self.world)]
+            flags = [heap.data_ptr(p) + self.flag_off[slot] for p in range(self.world)]
+            return (self.world, self.rank, self.epoch[slot] & 0xFFFFFFFF, data, flags, segs,
+                    self.flag_base[(key, name)], self.max_chunks)
+        return None
+
     # ------------------------------------------------------------- views
     def _slot_key(self, key):
         return key if key in ("embed", "tail") else key % 2
@@ -276,6 +360,10 @@ class Zero3LM:
         gather of the unit that follows in `direction` (+1 forward, -1 backward)."""
         cur = torch.cuda.current_stream()
         slot = self._slot_key(key)
+        if self.fused and key != "embed":
+            if self._gathered.get(slot) != key:
+                self._gather_fused(key)
+            return
         if not self.overlap:
             if self._gathered.get(slot) != key:
                 self._issue_gather(key, cur)
@@ -375,5 +463,7 @@ class Zero3LM:
         return out
 
     def close(self) -> None:
+        if self.fused:
+            K.set_b_gather(None)
         self.gsym.close()
         self.gradsym.close()
