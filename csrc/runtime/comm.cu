@@ -154,45 +154,47 @@ __device__ __forceinline__ uint4 pack16(const float (&acc)[8], float scale) {
 }
 
 // Peer loads are latency-bound (request / response over NVLink), so every
-// thread keeps kUnroll 16-byte vectors per peer in flight.
+// thread keeps several 16-byte vectors in flight: the reduction kernels are
+// instantiated per world size W and load U x W <= 8 vectors per pass, which
+// keeps them near 64 registers so they can share an SM with a GEMM CTA; the
+// push kernels keep kUnroll stores in flight.
 constexpr int kUnroll = 4;
 constexpr int kCommThreads = 256;
 
 // In-place two-shot all-reduce: this rank reduces its 1/W slice of the
 // 16-byte vectors from every peer, scales it and stores it back to every peer.
-template <bool BF16>
+template <bool BF16, int W>
 __global__ void __launch_bounds__(kCommThreads) allreduce_kernel(const ArArgs a) {
+  constexpr int U = W >= 8 ? 1 : 8 / W;  // U x W <= 8 vectors in flight per thread (<= 32 registers)
   const uint32_t e = next_epoch(a.pp, a.rank);
   if (!block_barrier(a.pp, a.rank, a.world, kInOff, e, a.status, 100)) {
     commit_epoch(a.pp, a.rank, e);
     return;
   }
   const long long n16 = a.n / (BF16 ? 8 : 4);
-  const long long per = (n16 + a.world - 1) / a.world;
+  const long long per = (n16 + W - 1) / W;
   const long long lo = per * a.rank;
   const long long hi = min(n16, lo + per);
   const long long G = (long long)gridDim.x * blockDim.x;
-  for (long long base = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; base < hi; base += kUnroll * G) {
-    uint4 v[kUnroll][kMaxWorld];
+  for (long long base = lo + blockIdx.x * (long long)blockDim.x + threadIdx.x; base < hi; base += U * G) {
+    uint4 v[U][W];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long long i = base + u * G;
 #pragma unroll
-      for (int p = 0; p < kMaxWorld; ++p)
-        if (p < a.world && i < hi) v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.off_bytes) + i);
+      for (int p = 0; p < W; ++p)
+        if (i < hi) v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.off_bytes) + i);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long long i = base + u * G;
       if (i >= hi) break;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int p = 0; p < kMaxWorld; ++p)
-        if (p < a.world) accum16<BF16>(acc, v[u][p]);
+      for (int p = 0; p < W; ++p) accum16<BF16>(acc, v[u][p]);
       const uint4 r = pack16<BF16>(acc, a.scale);
 #pragma unroll
-      for (int p = 0; p < kMaxWorld; ++p)
-        if (p < a.world) __stcg(reinterpret_cast<uint4*>(a.pp.data[p] + a.off_bytes) + i, r);
+      for (int p = 0; p < W; ++p) __stcg(reinterpret_cast<uint4*>(a.pp.data[p] + a.off_bytes) + i, r);
     }
   }
   block_barrier(a.pp, a.rank, a.world, kOutOff, e, a.status, 101);
@@ -212,35 +214,34 @@ struct RsArgs {
 // Reduce-scatter: rank r reads shard r of the input from every peer and
 // writes the scaled sum to its own output.  The closing barrier keeps every
 // input alive until all peers have read it.
-template <bool BF16>
+template <bool BF16, int W>
 __global__ void __launch_bounds__(kCommThreads) reduce_scatter_kernel(const RsArgs a) {
+  constexpr int U = W >= 8 ? 1 : 8 / W;
   const uint32_t e = next_epoch(a.pp, a.rank);
   if (!block_barrier(a.pp, a.rank, a.world, kInOff, e, a.status, 140)) {
     commit_epoch(a.pp, a.rank, e);
     return;
   }
-  const long long shard16 = a.n / a.world / (BF16 ? 8 : 4);
+  const long long shard16 = a.n / W / (BF16 ? 8 : 4);
   const long long lo = shard16 * a.rank;
   uint4* out = reinterpret_cast<uint4*>(a.pp.data[a.rank] + a.out_off_bytes);
   const long long G = (long long)gridDim.x * blockDim.x;
-  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < shard16; base += kUnroll * G) {
-    uint4 v[kUnroll][kMaxWorld];
+  for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < shard16; base += U * G) {
+    uint4 v[U][W];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long long i = base + u * G;
 #pragma unroll
-      for (int p = 0; p < kMaxWorld; ++p)
-        if (p < a.world && i < shard16)
-          v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.in_off_bytes) + lo + i);
+      for (int p = 0; p < W; ++p)
+        if (i < shard16) v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + a.in_off_bytes) + lo + i);
     }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       const long long i = base + u * G;
       if (i >= shard16) break;
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int p = 0; p < kMaxWorld; ++p)
-        if (p < a.world) accum16<BF16>(acc, v[u][p]);
+      for (int p = 0; p < W; ++p) accum16<BF16>(acc, v[u][p]);
       __stcg(out + i, pack16<BF16>(acc, a.scale));
     }
   }
@@ -396,7 +397,9 @@ struct RsSegArgs {
 // sum this rank's segments over every peer's gradient buffer (peer loads),
 // update fp32 master / moments and the bf16 shard in place.  The closing
 // barrier tells every rank its gradient buffer has been read.
+template <int W>
 __global__ void __launch_bounds__(kCommThreads) rs_adamw_segments_kernel(const RsSegArgs a) {
+  constexpr int U = W >= 4 ? 1 : 4 / W;  // float4 loads in flight: U x W <= 4 (plus the AdamW state)
   const uint32_t e = next_epoch(a.grads, a.rank);
   if (!block_barrier(a.grads, a.rank, a.world, kInOff, e, a.status, 160)) {
     commit_epoch(a.grads, a.rank, e);
@@ -412,22 +415,21 @@ __global__ void __launch_bounds__(kCommThreads) rs_adamw_segments_kernel(const R
     const long long len4 = a.t.len[sgi] / 4;
     const long long g4 = a.t.nat[sgi] / 4;
     const long long s4 = a.t.shard[sgi] / 4;
-    for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < len4; base += kUnroll * G) {
-      float4 gv[kUnroll][kMaxWorld];
+    for (long long base = blockIdx.x * (long long)blockDim.x + threadIdx.x; base < len4; base += U * G) {
+      float4 gv[U][W];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
+      for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int p = 0; p < kMaxWorld; ++p)
-          if (p < a.world && base + u * G < len4)
+        for (int p = 0; p < W; ++p)
+          if (base + u * G < len4)
             gv[u][p] = __ldcg(reinterpret_cast<const float4*>(a.grads.data[p] + a.g_off_bytes) + g4 + base + u * G);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
+      for (int u = 0; u < U; ++u) {
         const long long i = base + u * G;
         if (i >= len4) break;
         float gr[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int p = 0; p < kMaxWorld; ++p)
-          if (p < a.world) {
+        for (int p = 0; p < W; ++p) {
             gr[0] += gv[u][p].x;
             gr[1] += gv[u][p].y;
             gr[2] += gv[u][p].z;
@@ -571,6 +573,20 @@ static PeerPtrs peer_ptrs(const SymmetricHeap& h) {
 
 static int clamp_blocks(int blocks) { return blocks < 1 ? 1 : (blocks > kMaxBlocks ? kMaxBlocks : blocks); }
 
+// Launch `KERN<..., W>` for the runtime world size W in 1..8.
+#define UHFS_WORLD_DISPATCH(world, LAUNCH)                       \
+  switch (world) {                                             \
+    case 1: { constexpr int W = 1; LAUNCH; break; }            \
+    case 2: { constexpr int W = 2; LAUNCH; break; }            \
+    case 3: { constexpr int W = 3; LAUNCH; break; }            \
+    case 4: { constexpr int W = 4; LAUNCH; break; }            \
+    case 5: { constexpr int W = 5; LAUNCH; break; }            \
+    case 6: { constexpr int W = 6; LAUNCH; break; }            \
+    case 7: { constexpr int W = 7; LAUNCH; break; }            \
+    case 8: { constexpr int W = 8; LAUNCH; break; }            \
+    default: throw std::invalid_argument("world size must be 1..8"); \
+  }
+
 static void launch_allreduce(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
                              bool bf16, cudaStream_t s) {
   if (n % (bf16 ? 8 : 4) != 0 || off_bytes % 16 != 0)
@@ -584,8 +600,8 @@ static void launch_allreduce(const SymmetricHeap& h, long long off_bytes, long l
   a.rank = h.rank();
   a.world = h.world();
   a.status = device_status_ptr();
-  if (bf16) allreduce_kernel<true><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
-  else allreduce_kernel<false><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  if (bf16) UHFS_WORLD_DISPATCH(a.world, (allreduce_kernel<true, W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a)))
+  else UHFS_WORLD_DISPATCH(a.world, (allreduce_kernel<false, W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a)))
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -615,8 +631,8 @@ void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long lo
   a.rank = h.rank();
   a.world = h.world();
   a.status = device_status_ptr();
-  if (bf16) reduce_scatter_kernel<true><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
-  else reduce_scatter_kernel<false><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  if (bf16) UHFS_WORLD_DISPATCH(a.world, (reduce_scatter_kernel<true, W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a)))
+  else UHFS_WORLD_DISPATCH(a.world, (reduce_scatter_kernel<false, W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a)))
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -722,7 +738,7 @@ void comm_rs_adamw_segments(const SymmetricHeap& grads, long long g_off_bytes,
   a.rank = grads.rank();
   a.world = grads.world();
   a.status = device_status_ptr();
-  rs_adamw_segments_kernel<<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a);
+  UHFS_WORLD_DISPATCH(a.world, (rs_adamw_segments_kernel<W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a)))
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
