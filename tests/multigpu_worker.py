@@ -167,7 +167,9 @@ def case_zero3(rank: int, world: int) -> None:
         for name, slot in ref.flat.by_name.items():
             a = full[name].reshape(-1)
             b = ref.flat.master[slot.offset: slot.offset + slot.numel].float().cpu()
-            err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-6)).item()
+            # floor the scale: k_proj.bias has an exactly-zero gradient (a per-row
+            # shift of the scores) and stays at rounding-noise size
+            err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-3)).item()
             assert err < 2e-2, (tied, fused, name, err)
         z.close()
 

@@ -361,6 +361,9 @@ class Zero3LM:
         cur = torch.cuda.current_stream()
         slot = self._slot_key(key)
         if self.fused and key != "embed":
+            ev = self._events.pop(("g", key), None) if getattr(self, "_events", None) else None
+            if ev is not None:
+                cur.wait_event(ev)
             if self._gathered.get(slot) != key:
                 self._gather_fused(key)
             return
@@ -384,7 +387,8 @@ class Zero3LM:
             if 0 <= i < len(order):
                 nxt = order[i]
                 nslot = self._slot_key(nxt)
-                if self._gathered.get(nslot) != nxt and nxt != "embed":
+                # fused units are gathered by their first GEMM, never ahead
+                if self._gathered.get(nslot) != nxt and nxt != "embed" and not self.fused:
                     # everything issued so far (including the last reader of
                     # that slot) precedes the gather
                     comm.wait_stream(cur)
