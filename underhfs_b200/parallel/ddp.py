@@ -47,6 +47,13 @@ class BucketedAllReduce:
         self._enabled = True
         self._launched_any = False
         model.engine.grad_ready = self.on_ready
+        # UNDERHFS_DDP_TRACE=1: CUDA events around every bucket (eager steps
+        # only) and a per-step report of how much reduction time overlapped
+        # the backward kernels
+        import os
+
+        self.trace = os.environ.get("UNDERHFS_DDP_TRACE", "0") == "1"
+        self._trace_events: list = []
 
     def arm(self, enabled: bool = True) -> None:
         self._next = 0
@@ -59,7 +66,13 @@ class BucketedAllReduce:
         ev = torch.cuda.Event()
         ev.record(compute)
         self.stream.wait_event(ev)
+        if self.trace:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record(compute)  # compute reached this point (bucket final)
         with torch.cuda.stream(self.stream):
+            if self.trace:
+                s0 = torch.cuda.Event(enable_timing=True)
+                s0.record(self.stream)
             if self.use_nccl:
                 import torch.distributed as dist
 
@@ -70,6 +83,10 @@ class BucketedAllReduce:
             else:
                 core().comm_allreduce_f32(self.sym.heap, lo * 4, hi - lo, self.scale, self.blocks,
                                           self.stream.cuda_stream)
+            if self.trace:
+                s1 = torch.cuda.Event(enable_timing=True)
+                s1.record(self.stream)
+                self._trace_events.append((t0, s0, s1, hi - lo))
         self._launched_any = True
 
     def on_ready(self, lo: int, hi: int) -> None:
@@ -85,5 +102,20 @@ class BucketedAllReduce:
             blo, bhi = self.buckets[self._next]
             self._launch(blo, bhi)
             self._next += 1
+        if self.trace:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(torch.cuda.current_stream())  # backward kernels done
         torch.cuda.current_stream().wait_stream(self.stream)
         self._next = 0
+        if self.trace and self._trace_events:
+            done = torch.cuda.Event(enable_timing=True)
+            done.record(torch.cuda.current_stream())
+            done.synchronize()
+            first = self._trace_events[0][0]
+            busy = sum(s0.elapsed_time(s1) for _, s0, s1, _ in self._trace_events)
+            start_lag = sum(t0.elapsed_time(s0) for t0, s0, _, _ in self._trace_events)
+            tail = end.elapsed_time(done)
+            print(f"[ddp trace rank {self.rank}] buckets {len(self._trace_events)}, reduce kernels {busy:.3f} ms, "
+                  f"launch lag {start_lag:.3f} ms, from first bucket to backward end {first.elapsed_time(end):.3f} ms, "
+                  f"reduction tail after backward {tail:.3f} ms", flush=True)
+            self._trace_events = []

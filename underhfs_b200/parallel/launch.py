@@ -4,8 +4,10 @@
 spawns N copies of the script with RANK / LOCAL_RANK / WORLD_SIZE /
 MASTER_ADDR / MASTER_PORT set, forwards signals, and fails fast: when one
 rank exits non-zero the others are terminated and the launcher returns that
-exit code.  This is the module the reference's launch plan names but does not
-ship (distributed.py:47-55).
+exit code.  With ``--max-restarts K`` a failed job is started again (all
+ranks, ``UNDERHFS_RESTART_COUNT`` incremented) up to K times; the script is
+expected to resume from its last complete checkpoint.  This is the module the
+reference's launch plan names but does not ship (distributed.py:47-55).
 """
 
 from __future__ import annotations
@@ -25,15 +27,29 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--master-port", type=int, default=29511)
     ap.add_argument("--standalone", action="store_true")
     ap.add_argument("--timeout", type=float, default=0.0, help="kill all ranks after this many seconds (0 = none)")
+    ap.add_argument("--max-restarts", type=int, default=0, help="restart the whole job this many times on failure")
     ap.add_argument("script")
     ap.add_argument("args", nargs=argparse.REMAINDER)
     a = ap.parse_args(argv)
+    code = 0
+    for attempt in range(max(0, a.max_restarts) + 1):
+        code = _run_once(a, attempt)
+        if code == 0 or code == 130:
+            break
+        if attempt < a.max_restarts:
+            print(f"[launch] job failed with exit code {code}; restart {attempt + 1} of {a.max_restarts}",
+                  file=sys.stderr, flush=True)
+    return code
+
+
+def _run_once(a, attempt: int) -> int:
     n = max(1, a.nproc_per_node)
     procs: list[subprocess.Popen] = []
     for rank in range(n):
         env = dict(os.environ)
         env.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(n), LOCAL_WORLD_SIZE=str(n),
-                   MASTER_ADDR=a.master_addr, MASTER_PORT=str(a.master_port))
+                   MASTER_ADDR=a.master_addr, MASTER_PORT=str(a.master_port + 2 * attempt),
+                   UNDERHFS_RESTART_COUNT=str(attempt))
         cmd = [sys.executable, a.script, *a.args] if a.script.endswith(".py") else \
             [sys.executable, "-m", a.script, *a.args]
         procs.append(subprocess.Popen(cmd, env=env, start_new_session=True))
