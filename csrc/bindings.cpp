@@ -256,16 +256,24 @@ PYBIND11_MODULE(_core, m) {
     rmsnorm_bwd(dt, P<const void>(dy), P<const void>(x), P<const void>(w), P<const float>(rstd), P<const void>(dres),
                 P<void>(dx), P<float>(dw), rows, cols, S(s));
   });
-  m.def("embedding_fwd", [](int dt, uintptr_t ids, uintptr_t tok, uintptr_t pos, uintptr_t out, int rows, int dim,
-                            int seq_len, uintptr_t s) {
-    embedding_fwd(dt, P<const int64_t>(ids), P<const void>(tok), P<const void>(pos), P<void>(out), rows, dim, seq_len,
-                  S(s));
-  });
-  m.def("embedding_bwd", [](int dt, uintptr_t ids, uintptr_t dout, uintptr_t dtok, uintptr_t dpos, int rows, int dim,
-                            int seq_len, uintptr_t s) {
-    embedding_bwd(dt, P<const int64_t>(ids), P<const void>(dout), P<float>(dtok), P<float>(dpos), rows, dim, seq_len,
-                  S(s));
-  });
+  m.def(
+      "embedding_fwd",
+      [](int dt, uintptr_t ids, uintptr_t tok, uintptr_t pos, uintptr_t out, int rows, int dim, int seq_len,
+         uintptr_t s, long long vocab) {
+        embedding_fwd(dt, P<const int64_t>(ids), P<const void>(tok), P<const void>(pos), P<void>(out), rows, dim,
+                      seq_len, vocab, S(s));
+      },
+      py::arg("dt"), py::arg("ids"), py::arg("tok"), py::arg("pos"), py::arg("out"), py::arg("rows"), py::arg("dim"),
+      py::arg("seq_len"), py::arg("stream"), py::arg("vocab") = 0);
+  m.def(
+      "embedding_bwd",
+      [](int dt, uintptr_t ids, uintptr_t dout, uintptr_t dtok, uintptr_t dpos, int rows, int dim, int seq_len,
+         uintptr_t s, long long vocab) {
+        embedding_bwd(dt, P<const int64_t>(ids), P<const void>(dout), P<float>(dtok), P<float>(dpos), rows, dim,
+                      seq_len, vocab, S(s));
+      },
+      py::arg("dt"), py::arg("ids"), py::arg("dout"), py::arg("dtok"), py::arg("dpos"), py::arg("rows"),
+      py::arg("dim"), py::arg("seq_len"), py::arg("stream"), py::arg("vocab") = 0);
   m.def("softmax_ce", [](int dt, uintptr_t logits, long long ld, uintptr_t targets, uintptr_t loss_rows,
                          uintptr_t dlogits, int rows, int cols, float grad_scale, uintptr_t grad_scale_ptr,
                          uintptr_t s) {

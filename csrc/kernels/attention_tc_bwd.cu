@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       good = __shfl_sync(0xffffffffu, good, 0);
       if (!good) break;
       const int q0 = (i_start + t) * BQ;
+      if (!UHFS_CHECK(q0 < T && n0 < T, a.status, 303)) break;
       if (lane == 0) {
         uint8_t* sQ = sQD + st * Cfg::kStageBytes;
         uint8_t* sDO = sQ + Cfg::kTile;

@@ -49,6 +49,16 @@ __device__ __forceinline__ void report_error(DeviceStatus* st, int code, int whe
   atomicAdd(&st->count, 1);
 }
 
+// Debug index checks, compiled in with UNDERHFS_KERNEL_CHECKS=1 at build time
+// (-DUHFS_KERNEL_CHECKS): a failed check records kErrBounds with a site id and
+// evaluates to false so the caller skips the access.  Without the flag the
+// check is the constant true and costs nothing.
+#ifdef UHFS_KERNEL_CHECKS
+#define UHFS_CHECK(cond, st, where) ((cond) ? true : (::uhfs::report_error((st), ::uhfs::kErrBounds, (where)), false))
+#else
+#define UHFS_CHECK(cond, st, where) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -267,6 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tm, tn, kb0, kb1;
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * BM, n0 = tn * BN;
+        if (!UHFS_CHECK(m0 < args.M && n0 < args.N && kb0 < kb1 && kb1 <= args.kb_total, args.status, 12)) {
+          ok = false;
+          break;
+        }
         const bool gathered_b = args.ag.world > 0 && args.ag.b_flag_base >= 0;
         if (gathered_b && !B_MN && !wait_gathered_rows(args.ag, n0, min(args.N, n0 + BN), args.status)) {
           ok = false;

@@ -30,9 +30,10 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
 
 // ---- embedding (reference nn.py:184-217): token gather + optional learned position
 void embedding_fwd(int dtype, const int64_t* ids, const void* tok, const void* pos, void* out, int rows, int dim,
-                   int seq_len, cudaStream_t s);
+                   int seq_len, long long vocab, cudaStream_t s);
+// ids outside [0, vocab) (vocab > 0) are reported as kErrBounds and skipped
 void embedding_bwd(int dtype, const int64_t* ids, const void* dout, float* dtok, float* dpos, int rows, int dim,
-                   int seq_len, cudaStream_t s);
+                   int seq_len, long long vocab, cudaStream_t s);
 
 // ---- fused softmax cross-entropy (reference functional.py:20-76)
 // loss_rows[r] = -log softmax(logits[r])[target[r]];  if dlogits != null:

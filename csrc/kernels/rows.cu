@@ -10,6 +10,7 @@
 #include <type_traits>
 #include <stdexcept>
 
+#include "common.cuh"
 #include "kernels.h"
 #include "vec.cuh"
 
@@ -317,11 +318,18 @@ __global__ void rmsnorm_bwd_dw_kernel(const T* __restrict__ dy, const T* __restr
 template <typename T>
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ tok,
                                      const T* __restrict__ pos, T* __restrict__ out, int rows, int dim, int seq_len,
-                                     bool vec) {
+                                     bool vec, long long vocab, DeviceStatus* status) {
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
     const long long id = ids[row];
+    T* orow_bad = out + (long long)row * dim;
+    if (vocab > 0 && (id < 0 || id >= vocab)) {
+      // an id outside the table: record it and emit zeros instead of reading outside it
+      if (lane == 0) report_error(status, kErrBounds, 50);
+      for (int c = lane; c < dim; c += 32) orow_bad[c] = from_float<T>(0.f);
+      continue;
+    }
     const T* tr = tok + id * dim;
     const T* pr = pos != nullptr ? pos + (long long)(row % seq_len) * dim : nullptr;
     T* orow = out + (long long)row * dim;
@@ -342,11 +350,15 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const T* _
 template <typename T>
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ dout,
                                      float* __restrict__ dtok, float* __restrict__ dpos, int rows, int dim,
-                                     int seq_len, bool vec) {
+                                     int seq_len, bool vec, long long vocab, DeviceStatus* status) {
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
     const long long id = ids[row];
+    if (vocab > 0 && (id < 0 || id >= vocab)) {
+      if (lane == 0) report_error(status, kErrBounds, 51);
+      continue;
+    }
     const T* dr = dout + (long long)row * dim;
     float* tr = dtok != nullptr ? dtok + id * dim : nullptr;
     float* pr = dpos != nullptr ? dpos + (long long)(row % seq_len) * dim : nullptr;
@@ -416,7 +428,8 @@ __global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* 
                                                                       const int64_t* __restrict__ targets,
                                                                       float* __restrict__ loss_rows, T* dlogits,
                                                                       int cols, float grad_scale,
-                                                                      const float* grad_scale_ptr) {
+                                                                      const float* grad_scale_ptr,
+                                                                      DeviceStatus* status) {
   __shared__ float sm[kCeThreads / 32];
   const int row = blockIdx.x;
   const T* lr = logits + (long long)row * ld;
@@ -449,14 +462,16 @@ __global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* 
     }
   }
   const long long tgt = targets[row];
+  const bool tgt_ok = tgt >= 0 && tgt < cols;  // an invalid target is reported, never read
+  if (!tgt_ok && threadIdx.x == 0) report_error(status, kErrBounds, 52);
   // the target logit is read before the block barrier inside the sum
   // reduction, so an in-place dlogits (== logits) cannot overwrite it first
-  const float xt = threadIdx.x == 0 ? to_float<T>(lr[tgt]) : 0.f;
+  const float xt = (threadIdx.x == 0 && tgt_ok) ? to_float<T>(lr[tgt]) : 0.f;
   sum = block_reduce_sum(sum, sm);
   if (threadIdx.x == 0) {
     // -log(max(p_t, 1e-30)) as in the reference, computed in log space.
     const float nll = logf(sum) + mx - xt;
-    loss_rows[row] = fminf(nll, 69.07755279f);
+    loss_rows[row] = tgt_ok ? fminf(nll, 69.07755279f) : __int_as_float(0x7fc00000);  // NaN marks the bad row
   }
   if (dlogits == nullptr) return;
   if (grad_scale_ptr != nullptr) grad_scale *= *grad_scale_ptr;
@@ -483,7 +498,7 @@ __global__ void __launch_bounds__(kCeThreads) softmax_ce_kernel(const T* __restr
                                                                 const int64_t* __restrict__ targets,
                                                                 float* __restrict__ loss_rows, T* dlogits, int cols,
                                                                 float grad_scale, const float* grad_scale_ptr,
-                                                                bool vec) {
+                                                                bool vec, DeviceStatus* status) {
   const int row = blockIdx.x;
   const T* lr = logits + (long long)row * ld;
   __shared__ float sm_m[kCeThreads / 32], sm_s[kCeThreads / 32];
@@ -531,11 +546,17 @@ __global__ void __launch_bounds__(kCeThreads) softmax_ce_kernel(const T* __restr
   const float mx = row_max;
   const float inv = 1.0f / row_sum;
   const long long tgt = targets[row];
+  const bool tgt_ok = tgt >= 0 && tgt < cols;
   if (threadIdx.x == 0) {
-    const float xt = to_float<T>(lr[tgt]);
-    // -log(max(p_t, 1e-30)) as in the reference, computed in log space.
-    const float nll = logf(row_sum) + mx - xt;
-    loss_rows[row] = fminf(nll, 69.07755279f);
+    if (!tgt_ok) {
+      report_error(status, kErrBounds, 53);
+      loss_rows[row] = __int_as_float(0x7fc00000);
+    } else {
+      const float xt = to_float<T>(lr[tgt]);
+      // -log(max(p_t, 1e-30)) as in the reference, computed in log space.
+      const float nll = logf(row_sum) + mx - xt;
+      loss_rows[row] = fminf(nll, 69.07755279f);
+    }
   }
   if (dlogits == nullptr) return;
   if (grad_scale_ptr != nullptr) grad_scale *= *grad_scale_ptr;
@@ -718,21 +739,25 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
 }
 
 void embedding_fwd(int dtype, const int64_t* ids, const void* tok, const void* pos, void* out, int rows, int dim,
-                   int seq_len, cudaStream_t s) {
+                   int seq_len, long long vocab, cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(tok) && al16(pos) && al16(out) && (dim % 8 == 0);
+  DeviceStatus* st = device_status_ptr();
   UHFS_DISPATCH_DTYPE(dtype, embedding_fwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
-                                 ids, (const T*)tok, (const T*)pos, (T*)out, rows, dim, seq_len > 0 ? seq_len : 1, vec));
+                                 ids, (const T*)tok, (const T*)pos, (T*)out, rows, dim, seq_len > 0 ? seq_len : 1, vec,
+                                 vocab, st));
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
 
 void embedding_bwd(int dtype, const int64_t* ids, const void* dout, float* dtok, float* dpos, int rows, int dim,
-                   int seq_len, cudaStream_t s) {
+                   int seq_len, long long vocab, cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(dout) && al16(dtok) && al16(dpos) && (dim % 8 == 0);
+  DeviceStatus* st = device_status_ptr();
   UHFS_DISPATCH_DTYPE(dtype, embedding_bwd_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
-                                 ids, (const T*)dout, dtok, dpos, rows, dim, seq_len > 0 ? seq_len : 1, vec));
+                                 ids, (const T*)dout, dtok, dpos, rows, dim, seq_len > 0 ? seq_len : 1, vec, vocab,
+                                 st));
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -746,16 +771,19 @@ void softmax_ce_fwd_bwd(int dtype, const void* logits, long long ld, const int64
     if (dtype == DT_BF16)
       softmax_ce_reg_kernel<__nv_bfloat16><<<rows, kCeThreads, 0, s>>>(
           (const __nv_bfloat16*)logits, ld, targets, loss_rows, (__nv_bfloat16*)dlogits, cols, grad_scale,
-          grad_scale_ptr);
+          grad_scale_ptr, device_status_ptr());
     else
       softmax_ce_reg_kernel<__half><<<rows, kCeThreads, 0, s>>>((const __half*)logits, ld, targets, loss_rows,
-                                                               (__half*)dlogits, cols, grad_scale, grad_scale_ptr);
+                                                               (__half*)dlogits, cols, grad_scale, grad_scale_ptr,
+                                                               device_status_ptr());
     note_launch();
     UHFS_CUDA_CHECK(cudaGetLastError());
     return;
   }
+  DeviceStatus* st = device_status_ptr();
   UHFS_DISPATCH_DTYPE(dtype, softmax_ce_kernel<T><<<rows, kCeThreads, 0, s>>>(
-                                 (const T*)logits, ld, targets, loss_rows, (T*)dlogits, cols, grad_scale, grad_scale_ptr, vec));
+                                 (const T*)logits, ld, targets, loss_rows, (T*)dlogits, cols, grad_scale, grad_scale_ptr,
+                                 vec, st));
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

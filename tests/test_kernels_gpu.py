@@ -223,3 +223,27 @@ def test_reference_contract_kernels(K):
     stats = c.cuda_stream_stats()
     assert stats["non_blocking_streams"] == 1 and stats["launches"] > 0
     assert c.cuda_allocator_stats()["allocated_bytes"] > 0
+
+
+def test_out_of_range_ids_and_targets_are_reported_not_read(K):
+    """Invalid token ids / targets never index outside a table: the kernels
+    record kErrBounds (5) in the device status word and skip the row."""
+    tok = bf(torch.randn(100, 64, device="cuda"))
+    ids = torch.tensor([3, 100, -1, 7], device="cuda", dtype=torch.int64)
+    out = K.embedding(ids, tok, None, 4)
+    torch.cuda.synchronize()
+    st = K.core().device_status(True)
+    assert st["code"] == 5 and st["count"] >= 2, st
+    assert torch.equal(out[0].float(), tok[3].float()) and not out[1].float().any()
+    dtok = torch.zeros(100, 64, device="cuda")
+    K.embedding_backward(ids, out, dtok, None, 4)
+    torch.cuda.synchronize()
+    assert K.core().device_status(True)["code"] == 5
+    assert torch.equal(dtok[3], out[0].float())
+    logits = bf(torch.randn(3, 1024, device="cuda"))
+    tg = torch.tensor([5, 1024, -3], device="cuda", dtype=torch.int64)
+    loss = K.softmax_cross_entropy(logits, tg, None, 1.0)
+    torch.cuda.synchronize()
+    assert K.core().device_status(True)["code"] == 5
+    assert torch.isfinite(loss[0]) and torch.isnan(loss[1]) and torch.isnan(loss[2])
+    _status_ok()

@@ -31,6 +31,13 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
+def _check_flags() -> str:
+    """UNDERHFS_KERNEL_CHECKS=1 compiles the kernels' debug index checks in
+    (UHFS_CHECK in csrc/kernels/common.cuh); a failed check is reported in the
+    device status word and the access is skipped, never a trap."""
+    return "-DUHFS_KERNEL_CHECKS " if os.environ.get("UNDERHFS_KERNEL_CHECKS", "0") == "1" else ""
+
+
 def _pybind11_include() -> str:
     import pybind11
 
@@ -71,7 +78,7 @@ def _ninja_file() -> str:
         "ninja_required_version = 1.3",
         f"nvcc = {nvcc}",
         f"cxx = {cxx}",
-        f"nvflags = {' '.join(ARCH_FLAGS)} -lineinfo -O3 -std=c++17 --expt-relaxed-constexpr "
+        f"nvflags = {' '.join(ARCH_FLAGS)} -lineinfo -O3 -std=c++17 --expt-relaxed-constexpr {_check_flags()}"
         f"-Xcompiler -fPIC -Xcompiler -fvisibility=hidden -DNDEBUG {incs}",
         f"cxxflags = -O2 -std=c++17 -fPIC -fvisibility=hidden -DNDEBUG {incs}",
         f"ldflags = -shared {' '.join(ARCH_FLAGS)} -L{nccl_lib} -l:libnccl.so.2 "

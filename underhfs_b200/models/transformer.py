@@ -33,6 +33,7 @@ import torch
 
 from underhfs_b200.ops import kernels as K
 from underhfs_b200.parallel.flat import FlatBuffers, FlatLayout
+from underhfs_b200.utils import nvtx
 
 
 @dataclass(frozen=True)
@@ -236,6 +237,7 @@ class LMEngine:
         x = K.embedding(ids, self.E, self.P, T)
         saved_blocks = []
         for bi, blk in enumerate(self.blocks):
+            nvtx.push(f"fwd/block{bi}")
             self.unit_forward(bi)
             h1, r1 = K.rmsnorm(x, blk["ln1"], s.eps)
             qkv = K.linear_fwd(h1, blk["Wqkv"], blk["bqkv"])
@@ -246,6 +248,7 @@ class LMEngine:
             x2 = K.linear_fwd_resid(g, blk["W2"], blk["b2"], x1)
             saved_blocks.append((x, h1, r1, qkv, o, lse, x1, h2, r2, u, g))
             x = x2
+            nvtx.pop()
         self.unit_forward("tail")
         hf, rf = K.rmsnorm(x, self.lnf, s.eps)
         logits = K.linear_fwd(hf, self.Wh, None)
@@ -307,6 +310,7 @@ class LMEngine:
         del dl, dhf
         for bi in range(len(self.blocks) - 1, -1, -1):
             blk, saved = self.blocks[bi], sv["blocks"][bi]
+            nvtx.push(f"bwd/block{bi}")
             self.unit_backward_begin(bi)
             x, h1, r1, qkv, o, lse, x1, h2, r2, u, g = saved
             # MLP
@@ -338,6 +342,7 @@ class LMEngine:
             self.unit_backward_end(bi)
             if hook is not None:
                 hook(*blk["range"])
+            nvtx.pop()
         self.unit_backward_begin("embed")
         K.embedding_backward(sv["ids"], dx, self.gE, self.gP, T)
         self.unit_backward_end("embed")

@@ -232,13 +232,16 @@ def embedding(ids: torch.Tensor, tok: torch.Tensor, pos: torch.Tensor | None, se
     rows = ids.numel()
     dim = tok.shape[1]
     out = torch.empty((rows, dim), dtype=tok.dtype, device=tok.device)
-    core().embedding_fwd(dt(tok), ptr(ids), ptr(tok), ptr(pos), ptr(out), rows, dim, seq_len, stream())
+    core().embedding_fwd(dt(tok), ptr(ids), ptr(tok), ptr(pos), ptr(out), rows, dim, seq_len, stream(),
+                         tok.shape[0])
     return out
 
 
 def embedding_backward(ids, dout, dtok32, dpos32, seq_len):
     rows, dim = dout.shape
-    core().embedding_bwd(dt(dout), ptr(ids), ptr(dout), ptr(dtok32), ptr(dpos32), rows, dim, seq_len, stream())
+    vocab = dtok32.shape[0] if dtok32 is not None else 0
+    core().embedding_bwd(dt(dout), ptr(ids), ptr(dout), ptr(dtok32), ptr(dpos32), rows, dim, seq_len, stream(),
+                         vocab)
 
 
 def softmax_cross_entropy(logits: torch.Tensor, targets: torch.Tensor, dlogits: torch.Tensor | None,

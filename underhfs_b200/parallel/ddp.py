@@ -20,6 +20,7 @@ import torch
 
 from underhfs_b200.ops._lib import core
 from underhfs_b200.parallel.symmetric import SymmetricBuffer
+from underhfs_b200.utils import nvtx
 
 
 class BucketedAllReduce:
@@ -62,6 +63,7 @@ class BucketedAllReduce:
         self.model.engine.grad_ready = self.on_ready if enabled else None
 
     def _launch(self, lo: int, hi: int) -> None:
+        nvtx.push(f"allreduce/bucket[{lo},{hi})")
         compute = torch.cuda.current_stream()
         ev = torch.cuda.Event()
         ev.record(compute)
@@ -88,6 +90,7 @@ class BucketedAllReduce:
                 s1.record(self.stream)
                 self._trace_events.append((t0, s0, s1, hi - lo))
         self._launched_any = True
+        nvtx.pop()
 
     def on_ready(self, lo: int, hi: int) -> None:
         if not self._enabled:

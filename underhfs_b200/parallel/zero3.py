@@ -38,6 +38,7 @@ from underhfs_b200.models.transformer import LMEngine, LMSpec, build_layout
 from underhfs_b200.ops import kernels as K
 from underhfs_b200.ops._lib import core
 from underhfs_b200.parallel.symmetric import SymmetricBuffer
+from underhfs_b200.utils import nvtx
 
 
 def _round_up(n: int, a: int) -> int:
@@ -261,6 +262,10 @@ class Zero3LM:
             self.max_chunks = max(self.max_chunks, n)
 
     def _gather_fused(self, key) -> None:
+        with nvtx.nvtx_range(f"zero3/gather/{key}"):
+            self._gather_fused_impl(key)
+
+    def _gather_fused_impl(self, key) -> None:
         """Small parameters now (a barrier-bracketed gather kernel that also
         marks the unit boundary on every rank); the matrices are pushed by the
         first GEMM that reads them (gemm_ag)."""
@@ -423,6 +428,10 @@ class Zero3LM:
             torch.cuda.current_stream().wait_stream(self._comm())  # step boundary
 
     def _reduce(self, key) -> None:
+        with nvtx.nvtx_range(f"zero3/rs_adamw/{key}"):
+            self._reduce_impl(key)
+
+    def _reduce_impl(self, key) -> None:
         u = self.units[key]
         slot = self._slot_key(key)
         if self.overlap:
