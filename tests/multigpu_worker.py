@@ -174,11 +174,28 @@ def case_zero3(rank: int, world: int) -> None:
         z.close()
 
 
+def case_native(rank: int, world: int) -> None:
+    """The reference-style native NCCL group (host lists and device pointers),
+    bootstrapped through UNDERHFS_NCCL_UNIQUE_ID or the torch store."""
+    from underhfs_b200.distributed import native_nccl_group, policy_from_env
+
+    g = native_nccl_group(policy_from_env())
+    assert g.rank == rank and g.world_size == world
+    out = g.all_reduce_sum([1.0 + rank, 2.0])
+    assert out == [sum(1.0 + r for r in range(world)), 2.0 * world], out
+    x = torch.full((1 << 20,), float(rank + 1), device="cuda")
+    torch.cuda.synchronize()
+    g.all_reduce_ptr(x.data_ptr(), x.numel(), 0, 0)
+    torch.cuda.synchronize()
+    assert torch.all(x == sum(r + 1 for r in range(world))).item()
+    g.barrier()
+
+
 def main() -> int:
     case = sys.argv[1]
     rank, world = _setup()
     try:
-        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3}[case](rank, world)
+        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3, "native": case_native}[case](rank, world)
         dist.barrier()
         if rank == 0:
             print(f"OK {case}", flush=True)

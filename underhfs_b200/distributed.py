@@ -249,6 +249,28 @@ class ProcessGroup:
             self.synchronized = prev
 
 
+def native_nccl_group(policy: DistributedPolicy | None = None):
+    """The native ``_core.NcclProcessGroup`` (device-pointer collectives on its
+    own stream), bootstrapped like the reference's runtime
+    (distributed.py:190-201): from ``UNDERHFS_NCCL_UNIQUE_ID`` (hex) when set,
+    otherwise rank 0 creates an id and shares it through the torch.distributed
+    store (the process group must be initialised for that)."""
+    from underhfs_b200.ops._lib import core
+
+    pol = policy or policy_from_env()
+    c = core()
+    uid = os.environ.get("UNDERHFS_NCCL_UNIQUE_ID", "")
+    if not uid and pol.world_size > 1:
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("set UNDERHFS_NCCL_UNIQUE_ID (hex, from nccl_create_unique_id_hex) or initialise the "
+                               "process group first")
+        box = [c.nccl_create_unique_id_hex() if pol.rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        uid = box[0]
+    local = pol.local_rank if pol.local_rank is not None else pol.rank % max(1, torch.cuda.device_count())
+    return c.NcclProcessGroup(pol.rank, pol.world_size, uid, local)
+
+
 def process_group(policy: DistributedPolicy | None = None) -> ProcessGroup:
     return ProcessGroup(init_process_group(policy))
 
