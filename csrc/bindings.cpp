@@ -142,7 +142,7 @@ PYBIND11_MODULE(_core, m) {
       "gemm",
       [](int M, int N, int K, uintptr_t A, long long lda, bool a_mn, uintptr_t B, long long ldb, bool b_mn,
          uintptr_t C, long long ldc, int epi, uintptr_t bias, uintptr_t aux, long long ld_aux, uintptr_t aux_out,
-         long long ld_aux_out, int splits, int block_n, uintptr_t stream) {
+         long long ld_aux_out, int splits, int block_n, int cta_pair, uintptr_t stream) {
         GemmProblem p;
         p.M = M;
         p.N = N;
@@ -163,12 +163,13 @@ PYBIND11_MODULE(_core, m) {
         p.ld_aux_out = ld_aux_out;
         p.splits = splits;
         p.block_n = block_n;
+        p.cta_pair = cta_pair;
         gemm_bf16_tcgen05(p, S(stream));
       },
       py::arg("M"), py::arg("N"), py::arg("K"), py::arg("A"), py::arg("lda"), py::arg("a_mn"), py::arg("B"),
       py::arg("ldb"), py::arg("b_mn"), py::arg("C"), py::arg("ldc"), py::arg("epi"), py::arg("bias") = 0,
       py::arg("aux") = 0, py::arg("ld_aux") = 0, py::arg("aux_out") = 0, py::arg("ld_aux_out") = 0,
-      py::arg("splits") = 1, py::arg("block_n") = 0, py::arg("stream") = 0);
+      py::arg("splits") = 1, py::arg("block_n") = 0, py::arg("cta_pair") = -1, py::arg("stream") = 0);
   // GEMM whose B rows are gathered by the kernel itself (ZeRO-3): `segs` are
   // (src, dst_off_bytes, rows, row_bytes, flag_base) rows this rank pushes.
   m.def(

@@ -4,8 +4,8 @@
 //   * bounded mbarrier waits on %globaltimer (no wait can spin forever: on
 //     expiry the kernel records an error code in a device status word and the
 //     caller unwinds, freeing TMEM on the way out);
-//   * thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, never
-//     with .multicast::cluster) and the 5th-generation tensor core
+//   * thin inline-PTX wrappers for mbarrier, TMA (cp.async.bulk.tensor, no
+//     multicast form) and the 5th-generation tensor core
 //     (tcgen05.alloc / mma / commit / ld).
 #pragma once
 
@@ -384,6 +384,131 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, uint32_t a_mn, u
          | (b_mn << 16)         // B major
          | ((N >> 3) << 17)     // N / 8
          | ((M >> 4) << 24);    // M / 16
+}
+
+// ---------------------------------------------------------------------------
+// CTA pairs: a cluster of two CTAs on one TPC driving the tensor cores of
+// both SMs as one (tcgen05 .cta_group::2).  CTA rank 0 (the leader) issues
+// the MMAs; each CTA stages half of A and half of B in its own shared memory
+// at the same offsets, and each holds half of the accumulator rows in its
+// own TMEM.  Barriers of the other CTA are addressed through `mapa`.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at `p` in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t smem_cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs; orders shared-memory writes (barrier init, the
+// TMEM address) before the other CTA's accesses.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (either CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait_bounded for barriers that the other CTA of the pair signals.
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity, DeviceStatus* st, int err,
+                                                          int where) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (((++spins) & 255u) == 0u) {
+      if (globaltimer_ns() - t0 > kWaitBoundNs) {
+        report_error(st, err, where);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_warp_cluster(uint64_t* bar, uint32_t parity, DeviceStatus* st, int err,
+                                                       int where) {
+  const bool ok = mbar_wait_bounded_cluster(bar, parity, st, err, where);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// the leader CTA's mbarrier (`bar_cluster`: its shared::cluster address).
+// No multicast: each CTA loads its own half of the operands.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int coord0,
+                                                 int coord1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(coord0), "r"(coord1)
+      : "memory");
+}
+
+// Paired TMEM allocation: one warp of each CTA (the same warp index in both)
+// executes it; both CTAs receive the same column range.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (+)= A * B^T over the pair: M = 256 rows (128 per CTA), A and B halves
+// read from each CTA's shared memory at the descriptors' (common) offsets.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the mbarrier at `bar_cluster` (either CTA) once the pair MMAs
+// issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
 }
 
 // ---------------------------------------------------------------------------

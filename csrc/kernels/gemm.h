@@ -65,6 +65,7 @@ struct GemmProblem {
                       // ranges per CTA, partial tiles accumulated by the fp32 epilogue)
   int block_n = 0;    // 0 = choose, else 128 or 256
   int max_ctas = 0;   // 0 = one per SM
+  int cta_pair = -1;  // 256 x 256 tiles on CTA pairs: -1 = choose, 0 = off, 1 = on where supported
   GemmGather ag;      // fused all-gather of B rows (ZeRO-3), off by default
 };
 

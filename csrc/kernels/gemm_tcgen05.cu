@@ -205,6 +205,102 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
   }
 }
 
+// One accumulator tile, one epilogue warp: TMEM lanes quarter*32.. are rows
+// m0 + quarter*32 + lane of C (m0: first row held in this CTA's TMEM), the
+// warp takes columns [n0 + 32*c_begin, n0 + 32*c_end) of the BN-wide tile.
+// `release` runs once the warp holds its last TMEM chunk in registers (the
+// accumulator may then be reused).
+template <int BN, int EPI, class Release>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, const CUtensorMap* tmAuxOut,
+                                              uint32_t tmem_acc, int m0, int n0, int quarter, int ehalf, int lane,
+                                              uint8_t* box, Release release) {
+  constexpr int kBoxes = epi_boxes(EPI);
+  const int row = m0 + quarter * 32 + lane;
+  const bool row_ok = row < args.M;
+  const int c_begin = ehalf * (BN / 64), c_end = min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; ++c) {
+    const int col0 = n0 + c * 32;
+    float v[32];
+    const uint32_t taddr = tmem_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32);
+    tmem_ld_32x32b_x32(taddr, v);
+    tc_wait_ld();
+    if (c == c_end - 1) {
+      release();  // the whole accumulator of this warp is in registers
+    }
+    const int valid = min(32, args.N - col0);
+    if constexpr (EPI == GEMM_EPI_BF16 || EPI == GEMM_EPI_BIAS_GELU || EPI == GEMM_EPI_RESID) {
+      if (args.bias != nullptr) {
+        float b[32];
+        load_bf16x32(args.bias + col0, b, valid);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += b[j];
+      }
+    }
+    if constexpr (EPI == GEMM_EPI_RESID) {
+      if (row_ok) {
+        float r[32];
+        load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += r[j];
+      }
+    } else if constexpr (EPI == GEMM_EPI_DGELU) {
+      if (row_ok) {
+        float u[32];
+        load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad_fast(u[j]);
+      }
+    }
+    if constexpr (kBoxes > 0) {
+      // row `lane` of the warp's box: 4 chunks of 16 B at chunk ^ ((lane >> 1) & 3)
+      if (lane == 0) bulk_wait_group_read0();  // the previous stores have read the boxes
+      __syncwarp();
+      uint8_t* brow = box + lane * 64;
+      const int sw = (lane >> 1) & 3;
+      if constexpr (EPI == GEMM_EPI_BIAS_GELU) {
+        uint8_t* arow = brow + kEpiBox;  // pre-activation box (kept for the backward pass)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(arow + ((q ^ sw) << 4)) =
+              make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                         pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<uint4*>(brow + ((q ^ sw) << 4)) =
+            make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
+                       pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        // rows >= M and columns >= N fall outside the tensor map and are not written
+        tma_store_2d(tmC, box, col0, m0 + quarter * 32);
+        if constexpr (EPI == GEMM_EPI_BIAS_GELU) tma_store_2d(tmAuxOut, box + kEpiBox, col0, m0 + quarter * 32);
+        bulk_commit_group();
+      }
+    } else if constexpr (EPI == GEMM_EPI_F32_ACCUM) {
+      if (row_ok) {
+        float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q * 4 < valid) red_add_f32x4(dst + q * 4, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    } else {  // GEMM_EPI_F32_STORE
+      if (row_ok) {
+        float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q * 4 < valid)
+            *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    }
+  }
+  if (c_begin >= c_end) release();  // this warp has no columns in a narrow last tile
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -432,95 +528,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = tm * BM, n0 = tn * BN;
       if (!mbar_wait_warp(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
       tc_fence_after();
-      const int row = m0 + quarter * 32 + lane;
-      const bool row_ok = row < args.M;
-      const int c_begin = ehalf * (BN / 64), c_end = min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
-#pragma unroll 1
-      for (int c = c_begin; c < c_end; ++c) {
-        const int col0 = n0 + c * 32;
-        float v[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32);
-        tmem_ld_32x32b_x32(taddr, v);
-        tc_wait_ld();
-        if (c == c_end - 1) {
-          // the whole accumulator of this warp is in registers: release it
-          tc_fence_before();
-          mbar_arrive(&tempty[acc]);
-        }
-        const int valid = min(32, args.N - col0);
-        if constexpr (EPI == GEMM_EPI_BF16 || EPI == GEMM_EPI_BIAS_GELU || EPI == GEMM_EPI_RESID) {
-          if (args.bias != nullptr) {
-            float b[32];
-            load_bf16x32(args.bias + col0, b, valid);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += b[j];
-          }
-        }
-        if constexpr (EPI == GEMM_EPI_RESID) {
-          if (row_ok) {
-            float r[32];
-            load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += r[j];
-          }
-        } else if constexpr (EPI == GEMM_EPI_DGELU) {
-          if (row_ok) {
-            float u[32];
-            load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad_fast(u[j]);
-          }
-        }
-        if constexpr (kBoxes > 0) {
-          // row `lane` of the warp's box: 4 chunks of 16 B at chunk ^ ((lane >> 1) & 3)
-          if (lane == 0) bulk_wait_group_read0();  // the previous stores have read the boxes
-          __syncwarp();
-          uint8_t* brow = box + lane * 64;
-          const int sw = (lane >> 1) & 3;
-          if constexpr (EPI == GEMM_EPI_BIAS_GELU) {
-            uint8_t* arow = brow + kEpiBox;  // pre-activation box (kept for the backward pass)
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(arow + ((q ^ sw) << 4)) =
-                  make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
-                             pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(brow + ((q ^ sw) << 4)) =
-                make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
-                           pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            // rows >= M and columns >= N fall outside the tensor map and are not written
-            tma_store_2d(&tmC, box, col0, m0 + quarter * 32);
-            if constexpr (EPI == GEMM_EPI_BIAS_GELU) tma_store_2d(&tmAuxOut, box + kEpiBox, col0, m0 + quarter * 32);
-            bulk_commit_group();
-          }
-        } else if constexpr (EPI == GEMM_EPI_F32_ACCUM) {
-          if (row_ok) {
-            float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (q * 4 < valid) red_add_f32x4(dst + q * 4, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          }
-        } else {  // GEMM_EPI_F32_STORE
-          if (row_ok) {
-            float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (q * 4 < valid)
-                *reinterpret_cast<float4*>(dst + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          }
-        }
-      }
-      if (c_begin >= c_end) {  // this warp has no columns in a narrow last tile
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
-      }
+      epilogue_tile<BN, EPI>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * BN), m0, n0, quarter, ehalf, lane,
+                             box, [&] {
+                               tc_fence_before();
+                               mbar_arrive(&tempty[acc]);
+                             });
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -536,6 +548,241 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------ CTA-pair GEMM
+// 256 x 256 output tiles on a cluster of two CTAs (one TPC) with
+// tcgen05 .cta_group::2: the leader (rank 0) issues M = 256, N = 256 MMAs
+// whose A rows [0,128) and B rows [0,128) come from its own shared memory
+// and A rows [128,256), B rows [128,256) from its peer's.  Per SM that is
+// half the B bytes of the single-CTA 128 x 256 tile for the same MMA work,
+// so shared-memory bandwidth and L2 reads per FLOP drop by a third and six
+// 32 KB stages fit.  Each CTA's TMEM holds the 128 accumulator rows of its
+// own A half; both CTAs run the same epilogue on their rows.
+//   full[s]   leader only: both CTAs' TMA bytes (expect_tx by the leader)
+//   empty[s]  per CTA: the leader's MMA commit, sent to both CTAs
+//   tfull[a]  per CTA: the leader's commit after the last k-block
+//   tempty[a] leader only: 16 epilogue warps (8 per CTA) arrive
+// Used for the bf16 / fp32-store epilogues of tiles with M > 128 and
+// N > 128; split-K, stream-K and the fused all-gather stay on the
+// single-CTA kernel.
+constexpr int kPairThreads = 320;  // producer, MMA, 8 epilogue warps
+constexpr int kPairHalf = 128;     // rows of A and of B staged by each CTA
+constexpr int kPairStageBytes = 2 * kPairHalf * BK * 2;
+constexpr int kPairTmemCols = 512;  // 2 accumulators x 256 columns
+
+__host__ __device__ constexpr int pair_stages(int epi) {
+  return (227 * 1024 - 1280 - kEpiWarps * epi_boxes(epi) * kEpiBox) / kPairStageBytes < 6
+             ? (227 * 1024 - 1280 - kEpiWarps * epi_boxes(epi) * kEpiBox) / kPairStageBytes
+             : 6;
+}
+
+__host__ __device__ constexpr int pair_smem_bytes(int epi) {
+  return 1024 + pair_stages(epi) * kPairStageBytes + kEpiWarps * epi_boxes(epi) * kEpiBox + 256;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAuxOut,
+                     const GemmArgs args) {
+  constexpr int S = pair_stages(EPI);
+  constexpr int kABytes = kPairHalf * BK * 2;
+  constexpr uint32_t kIdesc = make_idesc(1 /*bf16*/, A_MN ? 1 : 0, B_MN ? 1 : 0, 2 * kPairHalf, 2 * kPairHalf);
+  constexpr int kBoxes = epi_boxes(EPI);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_align1024(smem_raw);  // same offsets in both CTAs
+  uint8_t* tiles = smem;
+  uint8_t* epi_stage = smem + S * kPairStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + kEpiWarps * kBoxes * kEpiBox);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* done = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int total = args.tiles_m * args.tiles_n;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if constexpr (kBoxes > 0) tma_prefetch_desc(&tmC);
+    if constexpr (kBoxes > 1) tma_prefetch_desc(&tmAuxOut);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * kEpiWarps);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  __syncwarp();
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kPairTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (elect_one_sync()) {
+      const uint32_t full_leader = smem_cluster_addr(full, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = (int)cluster_id_x(); ok && t < total; t += (int)cluster_count_x()) {
+        int tm, tn, split;
+        tile_coords(args, t, tm, tn, split);
+        const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf;
+        const int nb0 = tn * 2 * kPairHalf + (int)rank * kPairHalf;
+        for (int kb = 0; kb < args.kb_total; ++kb) {
+          if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, args.status, kErrWaitTimeoutEmpty, 13)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = tiles + stage * kPairStageBytes;
+          uint8_t* sB = sA + kABytes;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
+          const uint32_t bar = full_leader + stage * 8;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, bar, k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kPairHalf / 64; ++c) tma_load_2d_pair(sA + c * (64 * BK * 2), &tmA, bar, m0 + 64 * c, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(sB, &tmB, bar, k0, nb0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kPairHalf / 64; ++c) tma_load_2d_pair(sB + c * (64 * BK * 2), &tmB, bar, nb0 + 64 * c, k0);
+          }
+          issued_mask |= (1u << stage);
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // The leader's full barriers count both CTAs' bytes: once they have
+      // all flipped no copy of either CTA is still landing.
+      if (leader)
+        for (int s = 0; s < S; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait_bounded_cluster(&full[s], (issued_parity >> s) & 1u, args.status, kErrWaitTimeoutFull, 14);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader) {
+      if (elect_one_sync()) {
+        const uint32_t empty_l = smem_cluster_addr(empty, 0), empty_p = smem_cluster_addr(empty, 1);
+        const uint32_t tfull_l = smem_cluster_addr(tfull, 0), tfull_p = smem_cluster_addr(tfull, 1);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        for (int t = (int)cluster_id_x(); ok && t < total; t += (int)cluster_count_x()) {
+          if (!mbar_wait_bounded_cluster(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 23)) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * 2 * kPairHalf;
+          for (int kb = 0; kb < args.kb_total; ++kb) {
+            if (!mbar_wait_bounded_cluster(&full[stage], phase, args.status, kErrWaitTimeoutFull, 24)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(tiles + stage * kPairStageBytes);
+            const uint32_t b_base = a_base + kABytes;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              uint64_t adesc, bdesc;
+              if constexpr (!A_MN)
+                adesc = make_smem_desc(a_base + kk * 32, 16, 1024, kSwizzle128B);
+              else
+                adesc = make_smem_desc(a_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
+              if constexpr (!B_MN)
+                bdesc = make_smem_desc(b_base + kk * 32, 16, 1024, kSwizzle128B);
+              else
+                bdesc = make_smem_desc(b_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            // frees this stage in both CTAs once the MMAs retire
+            tc_commit_pair(empty_l + stage * 8);
+            tc_commit_pair(empty_p + stage * 8);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_commit_pair(tfull_l + acc * 8);
+          tc_commit_pair(tfull_p + acc * 8);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+        tc_commit_pair(smem_cluster_addr(done, 0));
+        tc_commit_pair(smem_cluster_addr(done, 1));
+        mbar_wait_bounded_cluster(done, 0, args.status, kErrWaitTimeoutAccum, 25);
+      }
+    } else if (lane == 0) {
+      // the peer's TMEM is written by the leader's MMAs: wait until they retired
+      mbar_wait_bounded_cluster(done, 0, args.status, kErrWaitTimeoutAccum, 26);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int ehalf = (warp - 2) >> 2;
+    uint8_t* box = epi_stage + (warp - 2) * kBoxes * kEpiBox;
+    const uint32_t tempty_leader = smem_cluster_addr(tempty, 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = (int)cluster_id_x(); t < total; t += (int)cluster_count_x()) {
+      int tm, tn, split;
+      tile_coords(args, t, tm, tn, split);
+      if (!mbar_wait_warp_cluster(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 31)) break;
+      tc_fence_after();
+      const uint32_t tempty_addr = tempty_leader + acc * 8;
+      epilogue_tile<2 * kPairHalf, EPI>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * 2 * kPairHalf),
+                                        tm * 2 * kPairHalf + (int)rank * kPairHalf, tn * 2 * kPairHalf, quarter,
+                                        ehalf, lane, box, [&] {
+                                          tc_fence_before();
+                                          __syncwarp();
+                                          if (lane == 0) mbar_arrive_cluster(tempty_addr);
+                                        });
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if constexpr (kBoxes > 0) {
+      if (lane == 0) bulk_wait_group0();
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while the other may still signal or read it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kPairTmemCols);
   }
 }
 
@@ -682,6 +929,101 @@ void dispatch_bn(const GemmProblem& p, cudaStream_t s) {
   throw std::runtime_error("gemm: unsupported (layout, epilogue) combination");
 }
 
+
+// Clusters of two CTAs that fit on the device at once (one CTA per SM).
+template <class K>
+int max_pair_clusters(K kern, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = num_sms() / 2;
+  }
+  return n;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const GemmProblem& p, cudaStream_t stream) {
+  constexpr int kSmem = pair_smem_bytes(EPI);
+  static_assert(kSmem <= 227 * 1024, "pair gemm shared memory");
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  static int clusters = 0;
+  if (clusters == 0) {
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    clusters = max_pair_clusters(kern, kSmem);
+  }
+  // Each CTA stages 128 rows of A and 128 rows of B per k-block.
+  CUtensorMap ta = A_MN ? make_tmap(p.A, p.M, p.K, p.lda, BK) : make_tmap(p.A, p.K, p.M, p.lda, kPairHalf);
+  CUtensorMap tb = B_MN ? make_tmap(p.B, p.N, p.K, p.ldb, BK) : make_tmap(p.B, p.K, p.N, p.ldb, kPairHalf);
+  GemmArgs a = {};
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.tiles_m = (p.M + 2 * kPairHalf - 1) / (2 * kPairHalf);
+  a.tiles_n = (p.N + 2 * kPairHalf - 1) / (2 * kPairHalf);
+  a.kb_total = (p.K + BK - 1) / BK;
+  a.splits = 1;
+  a.kb_per_split = a.kb_total;
+  a.stream_k = 0;
+  a.C = p.C;
+  a.ldc = p.ldc;
+  a.bias = p.bias;
+  a.aux = p.aux;
+  a.ld_aux = p.ld_aux;
+  a.aux_out = p.aux_out;
+  a.ld_aux_out = p.ld_aux_out;
+  a.status = device_status_ptr();
+  const int tiles = a.tiles_m * a.tiles_n;
+  int ncl = tiles < clusters ? tiles : clusters;
+  if (p.max_ctas > 0 && 2 * ncl > p.max_ctas) ncl = p.max_ctas / 2 > 0 ? p.max_ctas / 2 : 1;
+  CUtensorMap tc{}, taux{};
+  if constexpr (epi_boxes(EPI) > 0) tc = make_out_tmap(p.C, p.N, p.M, p.ldc);
+  if constexpr (epi_boxes(EPI) > 1) taux = make_out_tmap(p.aux_out, p.N, p.M, p.ld_aux_out);
+  kern<<<2 * ncl, kPairThreads, kSmem, stream>>>(ta, tb, tc, taux, a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+// true if the CTA-pair kernel took the problem
+bool dispatch_pair(const GemmProblem& p, cudaStream_t s) {
+  const bool am = p.a_mn, bm = p.b_mn;
+  switch (p.epi) {
+    case GEMM_EPI_BF16:
+      if (!am && !bm) return launch_pair<false, false, GEMM_EPI_BF16>(p, s), true;
+      if (!am && bm) return launch_pair<false, true, GEMM_EPI_BF16>(p, s), true;
+      if (am && !bm) return launch_pair<true, false, GEMM_EPI_BF16>(p, s), true;
+      return launch_pair<true, true, GEMM_EPI_BF16>(p, s), true;
+    case GEMM_EPI_BIAS_GELU:
+      if (!am && !bm) return launch_pair<false, false, GEMM_EPI_BIAS_GELU>(p, s), true;
+      break;
+    case GEMM_EPI_RESID:
+      if (!am && !bm) return launch_pair<false, false, GEMM_EPI_RESID>(p, s), true;
+      if (!am && bm) return launch_pair<false, true, GEMM_EPI_RESID>(p, s), true;
+      break;
+    case GEMM_EPI_DGELU:
+      if (!am && bm) return launch_pair<false, true, GEMM_EPI_DGELU>(p, s), true;
+      break;
+    case GEMM_EPI_F32_STORE:
+      if (!am && !bm) return launch_pair<false, false, GEMM_EPI_F32_STORE>(p, s), true;
+      if (!am && bm) return launch_pair<false, true, GEMM_EPI_F32_STORE>(p, s), true;
+      if (am && bm) return launch_pair<true, true, GEMM_EPI_F32_STORE>(p, s), true;
+      break;
+    default:
+      break;
+  }
+  return false;
+}
+
+bool pair_default() {
+  static const bool on = [] {
+    const char* e = getenv("UHFS_GEMM_PAIR");
+    return e != nullptr && std::string(e) == "1";
+  }();
+  return on;
+}
 }  // namespace
 
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
@@ -726,6 +1068,12 @@ void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {
     throw std::runtime_error("gemm: fp32 ldc must be a multiple of 4");
   int bn = p.block_n;
   if (bn != 128 && bn != 256) bn = (p.N <= 128) ? 128 : 256;
+  // CTA pairs: 256 x 256 tiles for one-pass (no split-K / stream-K) bf16 and
+  // fp32-store epilogues without a fused gather, when both M and N exceed one
+  // 128-row tile
+  const bool pair_ok = p.epi != GEMM_EPI_F32_ACCUM && p.ag.world == 0 && p.M > 128 && p.N > 128 && bn == 256;
+  const bool want_pair = p.cta_pair == 1 || (p.cta_pair < 0 && pair_default());
+  if (pair_ok && want_pair && dispatch_pair(p, stream)) return;
   if (bn == 256) dispatch_bn<256>(p, stream);
   else dispatch_bn<128>(p, stream);
 }

@@ -76,6 +76,53 @@ def test_gemm_dgrad_wgrad(K, M, N, K_):
     _status_ok()
 
 
+PAIR_SHAPES = [(300, 264, 200), (777, 1032, 1000), (2048, 2304, 768), (1536, 4096, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K_", PAIR_SHAPES)
+def test_gemm_cta_pair_layouts_and_epilogues(K, M, N, K_):
+    """256 x 256 tiles on CTA pairs (tcgen05 cta_group::2): every operand
+    layout and epilogue the pair kernel takes, ragged M / N / K edges."""
+    dev = "cuda"
+
+    def run(a, lda, a_mn, b, ldb, b_mn, epi, **kw):
+        dt = torch.float32 if epi == K.EPI_F32_STORE else torch.bfloat16
+        c = torch.empty(M, N, device=dev, dtype=dt)
+        K.gemm_raw(M, N, K_, a, lda, a_mn, b, ldb, b_mn, c, N, epi, cta_pair=1, **kw)
+        return c
+
+    xa = bf(torch.randn(M, K_, device=dev))
+    xb = bf(torch.randn(N, K_, device=dev) / math.sqrt(K_))
+    at, bt = xa.t().contiguous(), xb.t().contiguous()  # MN-major copies
+    ref = xa.float() @ xb.float().t()
+    for a, lda, a_mn in ((xa, K_, False), (at, M, True)):
+        for b, ldb, b_mn in ((xb, K_, False), (bt, N, True)):
+            assert O.rel_err(run(a, lda, a_mn, b, ldb, b_mn, K.EPI_BF16), ref) < 2e-2, (a_mn, b_mn)
+    assert O.rel_err(run(xa, K_, False, xb, K_, False, K.EPI_F32_STORE), ref) < 1e-2
+    assert O.rel_err(run(at, M, True, bt, N, True, K.EPI_F32_STORE), ref) < 1e-2
+    bias = bf(torch.randn(N, device=dev))
+    pre = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    g = run(xa, K_, False, xb, K_, False, K.EPI_BIAS_GELU, bias=bias, aux_out=pre, ld_aux_out=N)
+    assert O.rel_err(pre, ref + bias.float()) < 2e-2
+    assert O.rel_err(g, O.gelu_tanh(ref + bias.float())) < 2e-2
+    r = bf(torch.randn(M, N, device=dev))
+    y = run(xa, K_, False, xb, K_, False, K.EPI_RESID, bias=bias, aux=r, ld_aux=N)
+    assert O.rel_err(y, ref + bias.float() + r.float()) < 2e-2
+    y = run(xa, K_, False, bt, N, True, K.EPI_RESID, aux=r, ld_aux=N)
+    assert O.rel_err(y, ref + r.float()) < 2e-2
+    u = bf(torch.randn(M, N, device=dev))
+    gu = u.float().requires_grad_(True)
+    gd = torch.autograd.grad(O.gelu_tanh(gu).sum(), gu)[0]
+    y = run(xa, K_, False, bt, N, True, K.EPI_DGELU, aux=u, ld_aux=N)
+    assert O.rel_err(y, ref * gd) < 3e-2
+    # the same problem on one SM per tile agrees with the pair kernel
+    c1 = torch.empty(M, N, device=dev, dtype=torch.float32)
+    K.gemm_raw(M, N, K_, xa, K_, False, xb, K_, False, c1, N, K.EPI_F32_STORE, cta_pair=0)
+    c2 = run(xa, K_, False, xb, K_, False, K.EPI_F32_STORE)
+    assert torch.allclose(c1, c2, rtol=1e-5, atol=1e-4)
+    _status_ok()
+
+
 def test_matmul_bf16_and_f32(K):
     a = torch.randn(130, 72, device="cuda")
     b = torch.randn(72, 200, device="cuda")

@@ -48,8 +48,13 @@ def gemm_raw(
     ld_aux_out: int = 0,
     splits: int = 1,
     block_n: int = 0,
+    cta_pair: int = -1,
 ) -> None:
     """tcgen05 GEMM: C[M,N] (op)= sum_k A(m,k) B(n,k) with a fused epilogue.
+
+    ``cta_pair``: -1 lets the launcher choose between 128 x N tiles on one SM
+    and 256 x 256 tiles on a CTA pair (two SMs of a TPC); 0 / 1 force it
+    (1 only takes effect where the pair kernel supports the problem).
 
     When a B-gather resolver is installed (ZeRO-3 with fused gathers) and B
     lives in a gather slot, the launch carries the all-gather of B's rows.
@@ -63,7 +68,7 @@ def gemm_raw(
         return
     core().gemm(
         M, N, K, ptr(a), lda, a_mn, ptr(b), ldb, b_mn, ptr(c), ldc, epi, ptr(bias), ptr(aux), ld_aux,
-        ptr(aux_out), ld_aux_out, splits, block_n, stream(),
+        ptr(aux_out), ld_aux_out, splits, block_n, cta_pair, stream(),
     )
 
 
