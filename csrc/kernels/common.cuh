@@ -198,6 +198,11 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 }
 
 // Wait until this thread's bulk operations have completed.
+// At most one bulk group (the most recent) may still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
@@ -425,8 +430,10 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (either CTA).
+// Default semantics (release at CTA scope): used after tcgen05.wait::ld +
+// tcgen05.fence::before_thread_sync, which order the TMEM reads themselves.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {

@@ -205,22 +205,76 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
   }
 }
 
+// Epilogue operands that are read row-wise (the residual of GEMM_EPI_RESID,
+// the GELU input of GEMM_EPI_DGELU): each lane needs 64 bytes of its row per
+// 32-column chunk.  Chunk 0 is loaded before the warp waits for the
+// accumulator and chunk j + 1 while chunk j is processed, so the loads
+// overlap other work without keeping the whole tile in registers.
+template <int BN>
+struct AuxRegs {
+  uint4 r[BN / 64][4];
+};
+
+template <int EPI>
+constexpr bool epi_reads_aux() {
+  return EPI == GEMM_EPI_RESID || EPI == GEMM_EPI_DGELU;
+}
+
+__device__ __forceinline__ int epi_c_end(const GemmArgs& args, int BN, int n0, int ehalf) {
+  return min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
+}
+
+// Load chunk j of this warp's columns (zeros outside the matrix).
+template <int BN, int EPI>
+__device__ __forceinline__ void epi_load_aux(const GemmArgs& args, int m0, int n0, int quarter, int ehalf, int lane,
+                                             int j, uint4* r) {
+  if constexpr (epi_reads_aux<EPI>()) {
+    const int row = m0 + quarter * 32 + lane;
+    const int c = ehalf * (BN / 64) + j;
+    const int col0 = n0 + c * 32;
+    const bool ok = row < args.M && c < epi_c_end(args, BN, n0, ehalf);
+    const __nv_bfloat16* src = args.aux + (long long)row * args.ld_aux + col0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      r[q] = (ok && col0 + q * 8 < args.N) ? *reinterpret_cast<const uint4*>(src + q * 8) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+__device__ __forceinline__ void unpack_bf16x32(const uint4* raw, float* v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[q * 8 + 2 * j] = f.x;
+      v[q * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
 // One accumulator tile, one epilogue warp: TMEM lanes quarter*32.. are rows
 // m0 + quarter*32 + lane of C (m0: first row held in this CTA's TMEM), the
 // warp takes columns [n0 + 32*c_begin, n0 + 32*c_end) of the BN-wide tile.
 // `release` runs once the warp holds its last TMEM chunk in registers (the
-// accumulator may then be reused).
-template <int BN, int EPI, class Release>
+// accumulator may then be reused).  With kBufs == 2 consecutive chunks
+// alternate between two sets of store boxes (`seq` counts the warp's chunks),
+// so a chunk waits only for the stores issued two chunks earlier.
+template <int BN, int EPI, int kBufs, class Release>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, const CUtensorMap* tmAuxOut,
                                               uint32_t tmem_acc, int m0, int n0, int quarter, int ehalf, int lane,
-                                              uint8_t* box, Release release) {
+                                              uint8_t* box_base, uint32_t& seq, AuxRegs<BN>& aux,
+                                              Release release) {
   constexpr int kBoxes = epi_boxes(EPI);
   const int row = m0 + quarter * 32 + lane;
   const bool row_ok = row < args.M;
-  const int c_begin = ehalf * (BN / 64), c_end = min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
-#pragma unroll 1
-  for (int c = c_begin; c < c_end; ++c) {
+  const int c_begin = ehalf * (BN / 64), c_end = epi_c_end(args, BN, n0, ehalf);
+#pragma unroll
+  for (int j = 0; j < BN / 64; ++j) {
+    const int c = c_begin + j;
+    if (c >= c_end) break;
     const int col0 = n0 + c * 32;
+    if (j + 1 < BN / 64) epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, j + 1, aux.r[j + 1 < BN / 64 ? j + 1 : j]);
     float v[32];
     const uint32_t taddr = tmem_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32);
     tmem_ld_32x32b_x32(taddr, v);
@@ -234,27 +288,30 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
         float b[32];
         load_bf16x32(args.bias + col0, b, valid);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += b[j];
+        for (int i = 0; i < 32; ++i) v[i] += b[i];
       }
     }
     if constexpr (EPI == GEMM_EPI_RESID) {
-      if (row_ok) {
-        float r[32];
-        load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, r, valid);
+      float r[32];
+      unpack_bf16x32(aux.r[j], r);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] += r[j];
-      }
+      for (int i = 0; i < 32; ++i) v[i] += r[i];
     } else if constexpr (EPI == GEMM_EPI_DGELU) {
-      if (row_ok) {
-        float u[32];
-        load_bf16x32(args.aux + (long long)row * args.ld_aux + col0, u, valid);
+      float u[32];
+      unpack_bf16x32(aux.r[j], u);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad_fast(u[j]);
-      }
+      for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad_fast(u[i]);
     }
     if constexpr (kBoxes > 0) {
+      uint8_t* box = box_base + (kBufs == 2 ? (int)(seq & 1u) * kBoxes * kEpiBox : 0);
+      ++seq;
       // row `lane` of the warp's box: 4 chunks of 16 B at chunk ^ ((lane >> 1) & 3)
-      if (lane == 0) bulk_wait_group_read0();  // the previous stores have read the boxes
+      if (lane == 0) {
+        if constexpr (kBufs == 2)
+          bulk_wait_group_read1();  // the stores that last used this box set have read it
+        else
+          bulk_wait_group_read0();
+      }
       __syncwarp();
       uint8_t* brow = box + lane * 64;
       const int sw = (lane >> 1) & 3;
@@ -266,7 +323,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
               make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
                          pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_fast(v[j]);
+        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(v[i]);
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -522,17 +579,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* box = epi_stage + (warp - 2) * kBoxes * kEpiBox;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t seq = 0;
     UnitIter it = unit_begin(args);
     int tm, tn, kb0, kb1;
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * BM, n0 = tn * BN;
+      AuxRegs<BN> aux;
+      epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
       if (!mbar_wait_warp(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
       tc_fence_after();
-      epilogue_tile<BN, EPI>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * BN), m0, n0, quarter, ehalf, lane,
-                             box, [&] {
-                               tc_fence_before();
-                               mbar_arrive(&tempty[acc]);
-                             });
+      epilogue_tile<BN, EPI, 1>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * BN), m0, n0, quarter, ehalf,
+                                lane, box, seq, aux, [&] {
+                                  tc_fence_before();
+                                  mbar_arrive(&tempty[acc]);
+                                });
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -571,15 +631,18 @@ constexpr int kPairThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kPairHalf = 128;     // rows of A and of B staged by each CTA
 constexpr int kPairStageBytes = 2 * kPairHalf * BK * 2;
 constexpr int kPairTmemCols = 512;  // 2 accumulators x 256 columns
+constexpr int kPairBoxBufs = 2;     // epilogue store boxes double-buffered
+
+__host__ __device__ constexpr int pair_box_bytes(int epi) { return kPairBoxBufs * kEpiWarps * epi_boxes(epi) * kEpiBox; }
 
 __host__ __device__ constexpr int pair_stages(int epi) {
-  return (227 * 1024 - 1280 - kEpiWarps * epi_boxes(epi) * kEpiBox) / kPairStageBytes < 6
-             ? (227 * 1024 - 1280 - kEpiWarps * epi_boxes(epi) * kEpiBox) / kPairStageBytes
+  return (227 * 1024 - 1280 - pair_box_bytes(epi)) / kPairStageBytes < 6
+             ? (227 * 1024 - 1280 - pair_box_bytes(epi)) / kPairStageBytes
              : 6;
 }
 
 __host__ __device__ constexpr int pair_smem_bytes(int epi) {
-  return 1024 + pair_stages(epi) * kPairStageBytes + kEpiWarps * epi_boxes(epi) * kEpiBox + 256;
+  return 1024 + pair_stages(epi) * kPairStageBytes + pair_box_bytes(epi) + 256;
 }
 
 template <bool A_MN, bool B_MN, int EPI>
@@ -595,7 +658,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   uint8_t* smem = smem_align1024(smem_raw);  // same offsets in both CTAs
   uint8_t* tiles = smem;
   uint8_t* epi_stage = smem + S * kPairStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + kEpiWarps * kBoxes * kEpiBox);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + pair_box_bytes(EPI));
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -750,23 +813,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int ehalf = (warp - 2) >> 2;
-    uint8_t* box = epi_stage + (warp - 2) * kBoxes * kEpiBox;
+    uint8_t* box = epi_stage + (warp - 2) * kPairBoxBufs * kBoxes * kEpiBox;
     const uint32_t tempty_leader = smem_cluster_addr(tempty, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t seq = 0;
     for (int t = (int)cluster_id_x(); t < total; t += (int)cluster_count_x()) {
       int tm, tn, split;
       tile_coords(args, t, tm, tn, split);
+      const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf, n0 = tn * 2 * kPairHalf;
+      AuxRegs<2 * kPairHalf> aux;
+      epi_load_aux<2 * kPairHalf, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
       if (!mbar_wait_warp_cluster(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 31)) break;
       tc_fence_after();
       const uint32_t tempty_addr = tempty_leader + acc * 8;
-      epilogue_tile<2 * kPairHalf, EPI>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * 2 * kPairHalf),
-                                        tm * 2 * kPairHalf + (int)rank * kPairHalf, tn * 2 * kPairHalf, quarter,
-                                        ehalf, lane, box, [&] {
-                                          tc_fence_before();
-                                          __syncwarp();
-                                          if (lane == 0) mbar_arrive_cluster(tempty_addr);
-                                        });
+      epilogue_tile<2 * kPairHalf, EPI, kPairBoxBufs>(
+          args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * 2 * kPairHalf), m0, n0, quarter, ehalf, lane, box, seq,
+          aux, [&] {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_addr);
+          });
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -1017,12 +1084,23 @@ bool dispatch_pair(const GemmProblem& p, cudaStream_t s) {
   return false;
 }
 
-bool pair_default() {
+// UHFS_GEMM_PAIR=0 keeps every launch on the single-CTA kernel.
+bool pair_enabled() {
   static const bool on = [] {
     const char* e = getenv("UHFS_GEMM_PAIR");
-    return e != nullptr && std::string(e) == "1";
+    return e == nullptr || std::string(e) != "0";
   }();
   return on;
+}
+
+// Measured on B200 (16384-row Linear layers, K = 768..3072): the pair kernel
+// wins for plain bf16 / fp32 outputs at every K and for the residual / GELU /
+// dGELU epilogues once K >= 2048; with a short main loop those epilogues
+// (row-wise aux loads, two output tiles) bound the tile and the single-CTA
+// kernel's smaller tiles balance better.
+bool pair_preferred(const GemmProblem& p) {
+  if (!pair_enabled()) return false;
+  return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.K >= 2048;
 }
 }  // namespace
 
@@ -1072,7 +1150,7 @@ void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {
   // fp32-store epilogues without a fused gather, when both M and N exceed one
   // 128-row tile
   const bool pair_ok = p.epi != GEMM_EPI_F32_ACCUM && p.ag.world == 0 && p.M > 128 && p.N > 128 && bn == 256;
-  const bool want_pair = p.cta_pair == 1 || (p.cta_pair < 0 && pair_default());
+  const bool want_pair = p.cta_pair == 1 || (p.cta_pair < 0 && pair_preferred(p));
   if (pair_ok && want_pair && dispatch_pair(p, stream)) return;
   if (bn == 256) dispatch_bn<256>(p, stream);
   else dispatch_bn<128>(p, stream);
