@@ -115,21 +115,24 @@ __device__ __forceinline__ bool wait_gathered_rows(const GemmGather& g, int r0, 
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, int& tn, int& split);
 
-// Work units of one CTA, identical in the producer, MMA and epilogue roles.
-//   tiled:    units blockIdx.x, +gridDim.x, ... of tiles_m * tiles_n * splits
-//   stream-K: the k-block range [b*W/G, (b+1)*W/G) of the W = tiles * kb_total
-//             linearised (tile, k-block) space, cut at tile boundaries; each
-//             piece is accumulated into C by the fp32 epilogue.
+// Work units of one CTA (or CTA pair), identical in the producer, MMA and
+// epilogue roles; `idx` / `cnt` are the CTA's (pair's) index and count.
+//   tiled:    units idx, idx + cnt, ... of tiles_m * tiles_n * splits
+//   stream-K: the k-block range [idx*W/cnt, (idx+1)*W/cnt) of the
+//             W = tiles * kb_total linearised (tile, k-block) space, cut at
+//             tile boundaries; each piece is accumulated into C by the fp32
+//             epilogue.
 struct UnitIter {
   long long pos, end;
+  int stride;
 };
 
-__device__ __forceinline__ UnitIter unit_begin(const GemmArgs& a) {
+__device__ __forceinline__ UnitIter unit_begin(const GemmArgs& a, int idx, int cnt) {
   if (a.stream_k) {
     const long long total = (long long)a.tiles_m * a.tiles_n * a.kb_total;
-    return {(long long)blockIdx.x * total / gridDim.x, (long long)(blockIdx.x + 1) * total / gridDim.x};
+    return {(long long)idx * total / cnt, (long long)(idx + 1) * total / cnt, cnt};
   }
-  return {(long long)blockIdx.x, (long long)a.tiles_m * a.tiles_n * a.splits};
+  return {(long long)idx, (long long)a.tiles_m * a.tiles_n * a.splits, cnt};
 }
 
 __device__ __forceinline__ bool unit_next(const GemmArgs& a, UnitIter& it, int& tm, int& tn, int& kb0, int& kb1) {
@@ -146,7 +149,7 @@ __device__ __forceinline__ bool unit_next(const GemmArgs& a, UnitIter& it, int& 
   tile_coords(a, (int)it.pos, tm, tn, split);
   kb0 = split * a.kb_per_split;
   kb1 = min(kb0 + a.kb_per_split, a.kb_total);
-  it.pos += gridDim.x;
+  it.pos += it.stride;
   return true;
 }
 
@@ -416,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      UnitIter it = unit_begin(args);
+      UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
       int tm, tn, kb0, kb1;
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * BM, n0 = tn * BN;
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      UnitIter it = unit_begin(args);
+      UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
       int tm, tn, kb0, kb1;
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 20)) break;
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t seq = 0;
-    UnitIter it = unit_begin(args);
+    UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
     int tm, tn, kb0, kb1;
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * BM, n0 = tn * BN;
@@ -624,9 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   empty[s]  per CTA: the leader's MMA commit, sent to both CTAs
 //   tfull[a]  per CTA: the leader's commit after the last k-block
 //   tempty[a] leader only: 16 epilogue warps (8 per CTA) arrive
-// Used for the bf16 / fp32-store epilogues of tiles with M > 128 and
-// N > 128; split-K, stream-K and the fused all-gather stay on the
-// single-CTA kernel.
+// Used for every epilogue of problems with M > 128 and N > 128, one pass
+// per tile or stream-K (fp32 accumulate); classic split-K and the fused
+// all-gather stay on the single-CTA kernel.
 constexpr int kPairThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kPairHalf = 128;     // rows of A and of B staged by each CTA
 constexpr int kPairStageBytes = 2 * kPairHalf * BK * 2;
@@ -670,7 +673,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int total = args.tiles_m * args.tiles_n;
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
@@ -707,12 +709,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = (int)cluster_id_x(); ok && t < total; t += (int)cluster_count_x()) {
-        int tm, tn, split;
-        tile_coords(args, t, tm, tn, split);
+      UnitIter it = unit_begin(args, (int)cluster_id_x(), (int)cluster_count_x());
+      int tm, tn, kb0, kb1;
+      while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf;
         const int nb0 = tn * 2 * kPairHalf + (int)rank * kPairHalf;
-        for (int kb = 0; kb < args.kb_total; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded_cluster(&empty[stage], phase ^ 1u, args.status, kErrWaitTimeoutEmpty, 13)) {
             ok = false;
             break;
@@ -760,11 +762,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         bool ok = true;
-        for (int t = (int)cluster_id_x(); ok && t < total; t += (int)cluster_count_x()) {
+        UnitIter it = unit_begin(args, (int)cluster_id_x(), (int)cluster_count_x());
+        int tm, tn, kb0, kb1;
+        while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
           if (!mbar_wait_bounded_cluster(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 23)) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * 2 * kPairHalf;
-          for (int kb = 0; kb < args.kb_total; ++kb) {
+          for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait_bounded_cluster(&full[stage], phase, args.status, kErrWaitTimeoutFull, 24)) {
               ok = false;
               break;
@@ -783,7 +787,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 bdesc = make_smem_desc(b_base + kk * 32, 16, 1024, kSwizzle128B);
               else
                 bdesc = make_smem_desc(b_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
-              tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
             }
             // frees this stage in both CTAs once the MMAs retire
             tc_commit_pair(empty_l + stage * 8);
@@ -818,9 +822,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t seq = 0;
-    for (int t = (int)cluster_id_x(); t < total; t += (int)cluster_count_x()) {
-      int tm, tn, split;
-      tile_coords(args, t, tm, tn, split);
+    UnitIter it = unit_begin(args, (int)cluster_id_x(), (int)cluster_count_x());
+    int tm, tn, kb0, kb1;
+    while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf, n0 = tn * 2 * kPairHalf;
       AuxRegs<2 * kPairHalf> aux;
       epi_load_aux<2 * kPairHalf, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
@@ -1034,7 +1038,8 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   a.kb_total = (p.K + BK - 1) / BK;
   a.splits = 1;
   a.kb_per_split = a.kb_total;
-  a.stream_k = 0;
+  // splits == 0 with the fp32-accumulate epilogue selects stream-K over pairs
+  a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
   a.C = p.C;
   a.ldc = p.ldc;
   a.bias = p.bias;
@@ -1043,8 +1048,8 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   a.aux_out = p.aux_out;
   a.ld_aux_out = p.ld_aux_out;
   a.status = device_status_ptr();
-  const int tiles = a.tiles_m * a.tiles_n;
-  int ncl = tiles < clusters ? tiles : clusters;
+  const long long units = a.stream_k ? (long long)a.tiles_m * a.tiles_n * a.kb_total : (long long)a.tiles_m * a.tiles_n;
+  int ncl = units < clusters ? (int)units : clusters;
   if (p.max_ctas > 0 && 2 * ncl > p.max_ctas) ncl = p.max_ctas / 2 > 0 ? p.max_ctas / 2 : 1;
   CUtensorMap tc{}, taux{};
   if constexpr (epi_boxes(EPI) > 0) tc = make_out_tmap(p.C, p.N, p.M, p.ldc);
@@ -1073,6 +1078,10 @@ bool dispatch_pair(const GemmProblem& p, cudaStream_t s) {
     case GEMM_EPI_DGELU:
       if (!am && bm) return launch_pair<false, true, GEMM_EPI_DGELU>(p, s), true;
       break;
+    case GEMM_EPI_F32_ACCUM:
+      if (am && bm) return launch_pair<true, true, GEMM_EPI_F32_ACCUM>(p, s), true;
+      if (!am && bm) return launch_pair<false, true, GEMM_EPI_F32_ACCUM>(p, s), true;
+      break;
     case GEMM_EPI_F32_STORE:
       if (!am && !bm) return launch_pair<false, false, GEMM_EPI_F32_STORE>(p, s), true;
       if (!am && bm) return launch_pair<false, true, GEMM_EPI_F32_STORE>(p, s), true;
@@ -1100,7 +1109,7 @@ bool pair_enabled() {
 // kernel's smaller tiles balance better.
 bool pair_preferred(const GemmProblem& p) {
   if (!pair_enabled()) return false;
-  return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.K >= 2048;
+  return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.epi == GEMM_EPI_F32_ACCUM || p.K >= 2048;
 }
 }  // namespace
 
@@ -1146,10 +1155,11 @@ void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {
     throw std::runtime_error("gemm: fp32 ldc must be a multiple of 4");
   int bn = p.block_n;
   if (bn != 128 && bn != 256) bn = (p.N <= 128) ? 128 : 256;
-  // CTA pairs: 256 x 256 tiles for one-pass (no split-K / stream-K) bf16 and
-  // fp32-store epilogues without a fused gather, when both M and N exceed one
+  // CTA pairs: 256 x 256 tiles (one pass or stream-K; classic split-K stays
+  // on single CTAs) without a fused gather, when both M and N exceed one
   // 128-row tile
-  const bool pair_ok = p.epi != GEMM_EPI_F32_ACCUM && p.ag.world == 0 && p.M > 128 && p.N > 128 && bn == 256;
+  const bool pair_ok = (p.epi != GEMM_EPI_F32_ACCUM || p.splits <= 1) && p.ag.world == 0 && p.M > 128 &&
+                       p.N > 128 && bn == 256;
   const bool want_pair = p.cta_pair == 1 || (p.cta_pair < 0 && pair_preferred(p));
   if (pair_ok && want_pair && dispatch_pair(p, stream)) return;
   if (bn == 256) dispatch_bn<256>(p, stream);

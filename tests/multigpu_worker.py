@@ -52,10 +52,10 @@ def case_allreduce(rank: int, world: int) -> None:
     assert st["code"] == 0, st
 
 
-def _model(seed: int = 0):
+def _model(seed: int = 0, max_seq_len: int = 256):
     from underhfs_b200.nn import TransformerLM
 
-    m = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=2, heads=4,
+    m = TransformerLM(vocab_size=1024, max_seq_len=max_seq_len, features=256, hidden_features=1024, layers=2, heads=4,
                       tied=True, init="normal", seed=seed)
     m.to(f"cuda:{torch.cuda.current_device()}", dtype="bf16")
     return m
@@ -191,11 +191,47 @@ def case_native(rank: int, world: int) -> None:
     g.barrier()
 
 
+def case_cp(rank: int, world: int) -> None:
+    """Context parallelism: every rank holds a zigzag shard of the same
+    sequences; the group-averaged loss and gradients match one rank running
+    the whole sequences."""
+    from underhfs_b200.parallel.context import enable_context_parallel, shard_sequence
+
+    T = 1024
+    gen = torch.Generator().manual_seed(300)
+    ids = torch.randint(0, 1024, (2, T), generator=gen).cuda()
+    tg = torch.roll(ids, -1, 1)
+    ref_model = _model(max_seq_len=T)
+    ref_model.zero_grad()
+    ref_loss = ref_model(ids, tg)
+    ref_loss.backward()
+    ref = ref_model.flat.grads.clone()
+    model = _model(max_seq_len=T)
+    enable_context_parallel(model.engine, T)
+    model.zero_grad()
+    loss = model(shard_sequence(ids, rank, world), shard_sequence(tg, rank, world))
+    loss.backward()
+    torch.cuda.synchronize()
+    g = model.flat.grads.clone()
+    dist.all_reduce(g)
+    g /= world
+    lsum = torch.tensor([float(loss.item())], device="cuda")
+    dist.all_reduce(lsum)
+    lerr = abs(lsum.item() / world - ref_loss.item()) / abs(ref_loss.item())
+    gerr = ((g - ref).abs().max() / ref.abs().max()).item()
+    assert lerr < 2e-3 and gerr < 3e-2, (lerr, gerr)
+    from underhfs_b200.ops._lib import core
+
+    assert core().device_status(True)["code"] == 0
+
+
 def main() -> int:
     case = sys.argv[1]
     rank, world = _setup()
     try:
-        {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3, "native": case_native}[case](rank, world)
+        cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3,
+                 "native": case_native, "cp": case_cp}
+        cases[case](rank, world)
         dist.barrier()
         if rank == 0:
             print(f"OK {case}", flush=True)

@@ -115,6 +115,14 @@ def test_gemm_cta_pair_layouts_and_epilogues(K, M, N, K_):
     gd = torch.autograd.grad(O.gelu_tanh(gu).sum(), gu)[0]
     y = run(xa, K_, False, bt, N, True, K.EPI_DGELU, aux=u, ld_aux=N)
     assert O.rel_err(y, ref * gd) < 3e-2
+    # fp32 accumulate (weight-gradient layout), stream-K and one pass per tile
+    acc = torch.zeros(M, N, device=dev)
+    K.gemm_raw(M, N, K_, at, M, True, bt, N, True, acc, N, K.EPI_F32_ACCUM, splits=0, cta_pair=1)
+    assert O.rel_err(acc, ref) < 1e-2
+    K.gemm_raw(M, N, K_, at, M, True, bt, N, True, acc, N, K.EPI_F32_ACCUM, splits=1, cta_pair=1)
+    assert O.rel_err(acc, 2 * ref) < 1e-2
+    K.gemm_raw(M, N, K_, xa, K_, False, bt, N, True, acc, N, K.EPI_F32_ACCUM, splits=0, cta_pair=1)
+    assert O.rel_err(acc, 3 * ref) < 1e-2
     # the same problem on one SM per tile agrees with the pair kernel
     c1 = torch.empty(M, N, device=dev, dtype=torch.float32)
     K.gemm_raw(M, N, K_, xa, K_, False, xb, K_, False, c1, N, K.EPI_F32_STORE, cta_pair=0)

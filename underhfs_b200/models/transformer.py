@@ -161,6 +161,10 @@ class LMEngine:
         self.flat = flat
         self.causal = causal
         self.grad_ready: Callable[[int, int], None] | None = None
+        # context parallelism (parallel/context.py): attention over the group's
+        # sequence shards and the global positions of this rank's tokens
+        self.context_attention = None
+        self.positions: torch.Tensor | None = None
         self._saved: dict | None = None
         F = spec.features
         self.blocks = []
@@ -234,14 +238,19 @@ class LMEngine:
         H, D = s.heads, s.head_dim
         ids = ids.reshape(-1)
         self.unit_forward("embed")
-        x = K.embedding(ids, self.E, self.P, T)
+        # context parallelism: this rank's tokens sit at `positions` of the sequence
+        P = self.P if self.positions is None else self.P.index_select(0, self.positions)
+        x = K.embedding(ids, self.E, P, T)
         saved_blocks = []
         for bi, blk in enumerate(self.blocks):
             nvtx.push(f"fwd/block{bi}")
             self.unit_forward(bi)
             h1, r1 = K.rmsnorm(x, blk["ln1"], s.eps)
             qkv = K.linear_fwd(h1, blk["Wqkv"], blk["bqkv"])
-            o, lse = K.flash_attn_qkv(qkv, B, T, H, D, self.causal)
+            if self.context_attention is not None:
+                o, lse = self.context_attention.forward(qkv, B, T, H, D)
+            else:
+                o, lse = K.flash_attn_qkv(qkv, B, T, H, D, self.causal)
             x1 = K.linear_fwd_resid(o, blk["Wo"], blk["bo"], x)
             h2, r2 = K.rmsnorm(x1, blk["ln2"], s.eps)
             u, g = K.linear_fwd_gelu(h2, blk["W1"], blk["b1"])
@@ -330,7 +339,10 @@ class LMEngine:
             K.linear_wgrad_accum(dx1, o, blk["gWo"])
             if blk["gbo"] is not None:
                 K.colsum_accum(dx1, blk["gbo"])
-            dqkv = K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, self.causal)
+            if self.context_attention is not None:
+                dqkv = self.context_attention.backward(qkv, o, lse, do, B, T, H, D)
+            else:
+                dqkv = K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, self.causal)
             del do
             dh1 = K.linear_dgrad(dqkv, blk["Wqkv"])
             K.linear_wgrad_accum(dqkv, h1, blk["gWqkv"])
@@ -344,7 +356,12 @@ class LMEngine:
                 hook(*blk["range"])
             nvtx.pop()
         self.unit_backward_begin("embed")
-        K.embedding_backward(sv["ids"], dx, self.gE, self.gP, T)
+        if self.positions is None:
+            K.embedding_backward(sv["ids"], dx, self.gE, self.gP, T)
+        else:
+            gP = torch.zeros((T, self.gP.shape[1]), dtype=self.gP.dtype, device=self.gP.device)
+            K.embedding_backward(sv["ids"], dx, self.gE, gP, T)
+            self.gP.index_add_(0, self.positions, gP)
         self.unit_backward_end("embed")
         if hook is not None:
             hook(*self.embed_range)

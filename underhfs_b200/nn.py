@@ -537,9 +537,12 @@ class TransformerLM(Module):
         for name, p in self.named_parameters():
             p._rebind(flat.param(name), requires_grad=False, dtype=DType.BF16)
             object.__setattr__(p, "_main_grad", flat.grad(name))
-        hook = self._engine.grad_ready if self._engine is not None else None
+        old = self._engine
         engine = LMEngine(self.spec, flat)
-        engine.grad_ready = hook
+        if old is not None:  # keep the hooks installed on the previous engine
+            engine.grad_ready = old.grad_ready
+            engine.context_attention = old.context_attention
+            engine.positions = old.positions
         object.__setattr__(self, "_engine", engine)
 
     @property

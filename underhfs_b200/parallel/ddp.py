@@ -4,9 +4,10 @@ The engine's flat fp32 gradient buffer is re-homed into symmetric memory.
 Bucket boundaries are fixed at construction (every rank identical): equal
 ``bucket_bytes`` slices counted from the END of the buffer, because backward
 completes the last blocks first.  ``on_ready(lo, hi)`` (called by the engine
-after each block) launches every bucket that is now entirely final with the
-fused two-shot all-reduce kernel on a high-priority side stream, after an
-event recorded on the compute stream.  ``finish()`` flushes the remaining
+after each block) launches the buckets that are now entirely final -- as one
+launch over their contiguous range -- with the fused two-shot all-reduce
+kernel on a high-priority side stream, after an event recorded on the compute
+stream.  ``finish()`` flushes the remaining
 buckets and makes the compute stream wait for the side stream, so the
 optimizer step sees reduced gradients.
 
@@ -95,16 +96,19 @@ class BucketedAllReduce:
     def on_ready(self, lo: int, hi: int) -> None:
         if not self._enabled:
             return
+        # buckets that became final together are contiguous: one launch
+        first = self._next
         while self._next < len(self.buckets) and self.buckets[self._next][0] >= lo:
-            blo, bhi = self.buckets[self._next]
-            self._launch(blo, bhi)
             self._next += 1
+        if self._next > first:
+            self._launch(self.buckets[self._next - 1][0], self.buckets[first][1])
 
     def finish(self) -> None:
-        while self._next < len(self.buckets):
-            blo, bhi = self.buckets[self._next]
-            self._launch(blo, bhi)
-            self._next += 1
+        # the rest (the embeddings, final only after the last kernel of the
+        # backward) in one launch: no per-bucket synchronisation in the tail
+        if self._next < len(self.buckets):
+            self._launch(self.buckets[-1][0], self.buckets[self._next][1])
+            self._next = len(self.buckets)
         if self.trace:
             end = torch.cuda.Event(enable_timing=True)
             end.record(torch.cuda.current_stream())  # backward kernels done
