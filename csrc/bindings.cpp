@@ -406,6 +406,8 @@ PYBIND11_MODULE(_core, m) {
         flash_attn_bwd(p, S(s));
       });
 
+  m.def("set_attn_bwd_trace", [](uintptr_t buf) { set_attn_bwd_trace(P<unsigned long long>(buf)); });
+
   m.def("raster_iso", [](uintptr_t quads, uintptr_t colors, int n, uintptr_t order, uintptr_t rgba, int w, int h,
                          uintptr_t s) {
     raster_iso(P<const float>(quads), P<const unsigned int>(colors), n, P<unsigned int>(order),

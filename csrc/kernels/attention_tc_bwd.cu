@@ -8,14 +8,20 @@
 //               [64g, 64g+64).  Each thread loads its 64 S^T and 64 dP^T
 //               values with four TMEM loads and one wait, frees S^T / dP^T,
 //               and computes P^T = exp2(S^T*scale*log2e - lse) and
-//               dS^T = P^T (dP^T - delta), both written as bf16 into the
-//               swizzled shared tiles (warpgroup g fills sub-tile g); then
-//               lane r takes query row r, columns [gD/2, gD/2+D/2) of dQ_i
-//               from TMEM and adds them into the fp32 dQ accumulator in
-//               global memory (vector reductions); at the end the same split
-//               stores dK (scaled) and dV.
+//               dS^T = P^T (dP^T - delta), both as bf16: dS^T into the
+//               swizzled shared tile (warpgroup g fills sub-tile g), P^T for
+//               D = 64 into TMEM (the A operand of dV; shared memory for
+//               D = 128); at the end the same split stores dK (scaled) and
+//               dV.
 //   warp 8      TMA producer: K, V once; Q_i, dO_i per query block (ring),
 //               plus lse_i / delta_i into shared memory
+//   warps 12-15 dQ read-out: lane r of warp 12+q takes query row 32q + r of
+//               dQ_i from TMEM, stages it as swizzled fp32 boxes and adds
+//               them into the fp32 dQ accumulator with TMA reduce-add, off
+//               the compute warps' critical path (per-thread vector
+//               reductions of 32 different rows per warp instruction were
+//               measured to saturate the load/store pipe the compute warps
+//               need)
 //   warp 9      TMEM allocator + MMA issuer (one elected thread), per block i:
 //                 S^T  = K Q_i^T           M=128 keys, N=128 queries, K=D
 //                 dP^T = V dO_i^T          (same shape)
@@ -28,10 +34,15 @@
 //               compute warps hold block i in registers, so they overlap the
 //               softmax of block i.
 //
-// TMEM: S^T [0,128), dP^T [128,256), dV, dK, dQ after that (dQ reuses the
-// S^T columns when D = 128, which keeps that case in step order).
-// Registers: 384 threads launch with 168 each; warpgroup 2 gives back down to
-// 80 and the compute warpgroups take 208 (the host checks the launch count).
+// TMEM: S^T [0,128), dP^T [128,256), dV, dK, then for D = 64 dQ [384,448)
+// and P^T [448,512) (bf16 pairs); for D = 128 dQ reuses the S^T columns,
+// which keeps that case in step order.
+// Shared memory bandwidth bounds this kernel (every MMA operand but P^T is
+// read from it at 128 B/clk): with P^T in TMEM a 128 x 128 step of D = 64
+// moves about 300 KB through it.
+// Registers: 512 threads launch with 128 each; warpgroups 2 and 3 give back
+// down to 64 and the compute warpgroups take 192 (the host checks the launch
+// count).
 // Every wait is bounded.
 #include <cudaTypedefs.h>
 
@@ -53,29 +64,44 @@ namespace {
 constexpr int BK = 128;  // keys per CTA
 constexpr int BQ = 128;  // queries per step
 constexpr int kCompute = 256;      // warps 0..7
-constexpr int kThreads = 384;      // 3 warpgroups
-constexpr int kLaunchRegs = 168;   // 65536 / 384, rounded down to 8
-constexpr int kComputeRegs = 208;
-constexpr int kServiceRegs = 80;
-static_assert(2 * 128 * kComputeRegs + 128 * kServiceRegs <= kThreads * kLaunchRegs, "register split");
+constexpr int kReadout = 128;      // warps 12..15
+constexpr int kThreads = 512;      // 4 warpgroups
+constexpr int kLaunchRegs = 128;   // 65536 / 512
+constexpr int kComputeRegs = 192;
+constexpr int kServiceRegs = 64;
+static_assert(2 * 128 * kComputeRegs + 2 * 128 * kServiceRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct BwdCfg {
   static constexpr int kTile = 128 * D * 2;          // one [128][D] bf16 tile (D/64 swizzled sub-tiles)
-  static constexpr int kStages = (D == 64) ? 2 : 1;  // Q_i / dO_i ring depth
+  static constexpr int kStages = (D == 64) ? 4 : 1;  // Q_i / dO_i ring depth
+  static constexpr bool kPtTmem = (D == 64);          // P^T in TMEM (A operand of dV)
   static constexpr int kStageBytes = 2 * kTile;      // Q_i | dO_i
   static constexpr int kPT = BK * BQ * 2;            // P^T or dS^T tile (2 sub-tiles of 128 x 64)
   static constexpr int kVec = 2 * BQ * 4;            // lse_i | delta_i
-  static constexpr int kStage = 128 * 32 * 4;        // fp32 dQ staging box per warpgroup (128 rows x 32)
-  static constexpr int kSmem = 1024 + 2 * kTile + kStages * kStageBytes + 2 * kPT + kStages * kVec + 2 * kStage + 128;
+  static constexpr int kStage = 128 * 32 * 4;        // fp32 dQ staging box (128 rows x 32)
+  static constexpr int kStageBoxes = (D == 64) ? 1 : 2;
+  static constexpr int kSmem = 1024 + 2 * kTile + kStages * kStageBytes + (kPtTmem ? 1 : 2) * kPT + kStages * kVec +
+                               kStageBoxes * kStage + 256;
+  static_assert(kSmem <= 227 * 1024, "attention backward shared memory");
   static constexpr uint32_t kST = 0, kDPT = 128, kDV = 256, kDK = 256 + D;
   static constexpr uint32_t kDQ = (D == 64) ? 256 + 2 * D : 0;  // D=128: reuse S^T columns
-  // D=64: two dQ buffers (columns 384 and 448), so dQ of block t is read out
-  // while block t+1's softmax runs; D=128 has no room and reads it in place.
-  static constexpr int kDQBufs = (D == 64) ? 2 : 1;
+  static constexpr uint32_t kPTT = 256 + 3 * D;                  // D=64: P^T (64 columns of bf16 pairs)
+  static constexpr int kDQBufs = 1;
+  static_assert(!kPtTmem || kPTT + 64 <= 512, "P^T columns");
   static constexpr uint32_t kCols = 512;
 };
+
+// Optional per-step clock stamps (clock64 of the SM) for the CTAs of head 0
+// of batch 0: trace[(blockIdx.x * kTraceEvents + event) * kTraceSteps + step].
+// Off (nullptr) unless a buffer is installed with set_attn_bwd_trace.
+constexpr int kTraceEvents = 16, kTraceSteps = 64;
+enum BwdTraceEvent {
+  kTrStart = 0, kTrQdEmpty, kTrQdStored, kTrMmaS, kTrMmaGrads, kTrSFull, kTrSRegs, kTrMath, kTrPFull,
+  kTrDqFull, kTrDqDone, kTrEpiStart, kTrEpiEnd, kTrKvFull
+};
+unsigned long long* g_bwd_trace = nullptr;
 
 struct BwdArgs {
   int B, H, T;
@@ -87,7 +113,14 @@ struct BwdArgs {
   float* dq_accum;      // [B, T, H, D] fp32
   __nv_bfloat16* dqkv;  // [B*T, 3F]
   DeviceStatus* status;
+  unsigned long long* trace;
 };
+
+#define BWD_TRACE(ev, step)                                                                              \
+  do {                                                                                                   \
+    if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
+      a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
+  } while (0)
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -101,24 +134,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sK = smem;
   uint8_t* sV = sK + Cfg::kTile;
   uint8_t* sQD = sV + Cfg::kTile;                 // [S][Q | dO]
-  uint8_t* sPT = sQD + S * Cfg::kStageBytes;      // P^T
-  uint8_t* sDST = sPT + Cfg::kPT;                 // dS^T
-  float* sVec = reinterpret_cast<float*>(sDST + Cfg::kPT);  // [S][lse(128) | delta(128)]
-  uint8_t* sStage = reinterpret_cast<uint8_t*>(sVec) + S * Cfg::kVec;  // [2 warpgroups] fp32 dQ boxes
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 2 * Cfg::kStage);
+  uint8_t* sDST = sQD + S * Cfg::kStageBytes;     // dS^T
+  uint8_t* sPT = sDST + Cfg::kPT;                 // P^T (D = 128 only)
+  float* sVec = reinterpret_cast<float*>(sDST + (Cfg::kPtTmem ? 1 : 2) * Cfg::kPT);  // [S][lse(128) | delta(128)]
+  uint8_t* sStage = reinterpret_cast<uint8_t*>(sVec) + S * Cfg::kVec;  // [kStageBoxes] fp32 dQ boxes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + Cfg::kStageBoxes * Cfg::kStage);
   uint64_t* kv_full = bars;          // 1
-  uint64_t* qd_full = bars + 1;      // [2]
-  uint64_t* qd_empty = bars + 3;     // [2]
-  uint64_t* s_full = bars + 5;       // S^T and dP^T ready
-  uint64_t* s_free = bars + 6;       // S^T / dP^T held in registers by all compute threads
-  uint64_t* p_full = bars + 7;       // P^T / dS^T written
-  // one dQ ready / read barrier pair per dQ buffer, so that neither side can
-  // get two phases ahead of the other
-  uint64_t* dq_full = bars + 8;      // [2] dQ of a step ready (dQ MMAs done)
-  uint64_t* dq_free = bars + 10;     // [2] dQ of a step read out
-  uint64_t* pt_free = bars + 12;     // dV / dK MMAs of step i done: P^T / dS^T reusable
-  uint64_t* done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* qd_full = bars + 1;      // [S]
+  uint64_t* qd_empty = bars + 1 + S; // [S]
+  uint64_t* s_full = bars + 1 + 2 * S;   // S^T and dP^T ready
+  uint64_t* s_free = s_full + 1;     // S^T / dP^T held in registers by all compute threads
+  uint64_t* p_full = s_full + 2;     // P^T / dS^T written
+  uint64_t* dq_full = s_full + 3;    // dQ of a step ready (dQ MMAs done)
+  uint64_t* dq_free = s_full + 4;    // dQ of a step read out
+  uint64_t* pt_free = s_full + 5;    // dV / dK MMAs of step i done: P^T / dS^T reusable
+  uint64_t* done = s_full + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
@@ -137,16 +168,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_dq);
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < S; ++i) {
       mbar_init(&qd_full[i], 2);  // TMA bytes + the producer's lse / delta stores
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, kCompute);
     mbar_init(p_full, kCompute);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Cfg::kDQBufs; ++i) {
       mbar_init(&dq_full[i], 1);
-      mbar_init(&dq_free[i], kCompute);
+      mbar_init(&dq_free[i], kReadout);
     }
     mbar_init(pt_free, 1);
     mbar_init(done, 1);
@@ -169,8 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
-    bool issued[2] = {false, false};
-    uint32_t iph[2] = {0, 0};
+    uint32_t issued = 0, iph = 0;  // bit s: stage s has a load in flight / its phase
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * Cfg::kTile);
       for (int kd = 0; kd < KD; ++kd) {
@@ -185,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) good = mbar_wait_bounded(&qd_empty[st], ph ^ 1u, a.status, kErrWaitTimeoutEmpty, 300);
       good = __shfl_sync(0xffffffffu, good, 0);
       if (!good) break;
+      if (lane == 0) BWD_TRACE(kTrQdEmpty, t);
       const int q0 = (i_start + t) * BQ;
       if (!UHFS_CHECK(q0 < T && n0 < T, a.status, 303)) break;
       if (lane == 0) {
@@ -195,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sQ + kd * (BQ * 128), &tm_qkv, &qd_full[st], (int)(h * D + kd * 64), row0 + q0);
           tma_load_2d(sDO + kd * (BQ * 128), &tm_do, &qd_full[st], (int)(h * D + kd * 64), row0 + q0);
         }
-        issued[st] = true;
-        iph[st] = ph;
+        issued |= 1u << st;
+        iph = (iph & ~(1u << st)) | (ph << st);
       }
       // lse / delta of this query block: all loads in flight at once, then the
       // stores, ordered before the second arrival on qd_full
@@ -214,12 +245,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         vec[BQ + k * 32 + lane] = dv[k];
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&qd_full[st]);
+      if (lane == 0) {
+        mbar_arrive(&qd_full[st]);
+        BWD_TRACE(kTrQdStored, t);
+      }
     }
     if (lane == 0) {
       mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 301);
       for (int s2 = 0; s2 < S; ++s2)
-        if (issued[s2]) mbar_wait_bounded(&qd_full[s2], iph[s2], a.status, kErrWaitTimeoutFull, 302);
+        if (issued & (1u << s2)) mbar_wait_bounded(&qd_full[s2], (iph >> s2) & 1u, a.status, kErrWaitTimeoutFull, 302);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -236,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](int t) -> bool {
         const int st = t % S;
         if (!mbar_wait_bounded(&qd_full[st], (uint32_t)(t / S) & 1u, a.status, kErrWaitTimeoutFull, 311)) return false;
+        BWD_TRACE(kTrMmaS, t);
         tc_fence_after();
         const uint32_t q16 = qd16 + st * (Cfg::kStageBytes >> 4), do16 = q16 + (Cfg::kTile >> 4);
 #pragma unroll 1
@@ -269,13 +304,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t aoff = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
           const uint32_t boff = (kk * 16 * 128) >> 4;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc_mma_f16(tmem + Cfg::kDV, kmaj + pt16 + aoff, mnmaj + do16 + boff, id_kv, acc);
+          if constexpr (Cfg::kPtTmem)
+            tc_mma_f16_ts(tmem + Cfg::kDV, tmem + Cfg::kPTT + (uint32_t)(kk * 8), mnmaj + do16 + boff, id_kv, acc);
+          else
+            tc_mma_f16(tmem + Cfg::kDV, kmaj + pt16 + aoff, mnmaj + do16 + boff, id_kv, acc);
           tc_mma_f16(tmem + Cfg::kDK, kmaj + dst16 + aoff, mnmaj + q16 + boff, id_kv, acc);
         }
         tc_commit(pt_free);
         tc_commit(&qd_empty[st]);
       };
       bool ok = mbar_wait_bounded(kv_full, 0, a.status, kErrWaitTimeoutFull, 310);
+      BWD_TRACE(kTrKvFull, 0);
       if (D == 64) {
         // S^T / dP^T of block t+1 are issued before the gradients of block t
         ok = ok && issue_s(0);
@@ -294,6 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          BWD_TRACE(kTrMmaGrads, t);
           tc_fence_after();
           issue_grads(t);
         }
@@ -325,50 +365,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key = n0 + r;
     const bool kvalid = key < T;
     const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* pt_row = sPT + half * (128 * 128) + r * 128;
+    [[maybe_unused]] uint8_t* pt_row = sPT + half * (128 * 128) + r * 128;
     uint8_t* dst_row = sDST + half * (128 * 128) + r * 128;
-    uint8_t* stage = sStage + half * Cfg::kStage;
-    const bool leader = quarter == 0 && lane == 0;  // issues this warpgroup's TMA reductions
-    // Failures are warp-uniform but not warpgroup-uniform, so every thread
-    // runs the same sequence of named barriers for every step; after a failed
-    // wait a thread only skips the work.
+    // Failures are warp-uniform (mbar_wait_warp); after a failed wait a warp
+    // skips the work but keeps arriving where the others expect it.
     bool ok = true;
-    // dQ of block tt: TMEM -> registers -> swizzled fp32 box -> TMA
-    // reduce-add into the fp32 accumulator.  Rows past T add zeros (P is 0).
-    auto readout = [&](int tt) {
-      const int q0 = (i_start + tt) * BQ;
-      const int bi = tt % Cfg::kDQBufs;
-      const uint32_t buf = (uint32_t)(bi * D);
-      if (ok && !mbar_wait_warp(&dq_full[bi], (uint32_t)(tt / Cfg::kDQBufs) & 1u, a.status, kErrWaitTimeoutAccum, 322))
-        ok = false;
-#pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t v[32];
-        if (ok) {
-          tc_fence_after();
-          tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + buf + half * (D / 2) + c * 32, v);
-          tmem_wait_ld_regs<32>(v);
-          if (c == D / 64 - 1) {
-            tc_fence_before();
-            mbar_arrive(&dq_free[bi]);  // this dQ buffer may be overwritten
-          }
-        }
-        if (leader) bulk_wait_group_read0();  // the previous reduction has read the box
-        named_barrier_sync(1 + half, 128);
-        if (ok) {
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch)
-            *reinterpret_cast<uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4)) =
-                make_uint4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
-          fence_proxy_async_smem();
-        }
-        named_barrier_sync(1 + half, 128);
-        if (leader && ok) {
-          tma_reduce_add_2d(&tm_dq, stage, h * D + half * (D / 2) + c * 32, row0 + q0);
-          bulk_commit_group();
-        }
-      }
-    };
+    const bool tracer = warp == 0 && lane == 0;
+    if (tracer) BWD_TRACE(kTrStart, 0);
     for (int t = 0; t < steps; ++t) {
       const int st = t % S;
       const uint32_t tp = t & 1;
@@ -377,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && (!mbar_wait_warp(&qd_full[st], (t / S) & 1, a.status, kErrWaitTimeoutFull, 320) ||
                  !mbar_wait_warp(s_full, tp, a.status, kErrWaitTimeoutAccum, 321)))
         ok = false;
+      if (tracer) BWD_TRACE(kTrSFull, t);
       if (ok) {
         tc_fence_after();
         uint32_t sv[64], pv[64];
@@ -388,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld_regs<64>(pv);
         tc_fence_before();
         mbar_arrive(s_free);  // S^T / dP^T may be overwritten
+        if (tracer) BWD_TRACE(kTrSRegs, t);
         const float4* lse4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + half * 64);
         const float4* dlt4 = reinterpret_cast<const float4*>(sVec + st * (2 * BQ) + BQ + half * 64);
         // causal diagonal block: query column qi is visible for this key when qi >= key - q0
@@ -411,33 +416,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           hd[g * 2] = pack_bf16x2(ds[0], ds[1]);
           hd[g * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
         }
+        if (tracer) BWD_TRACE(kTrMath, t);
         // P^T / dS^T tiles are free once the gradient MMAs of block t-1 finished
         if (t > 0 && !mbar_wait_warp(pt_free, (uint32_t)(t - 1) & 1u, a.status, kErrWaitTimeoutAccum, 323))
           ok = false;
         if (ok) {
+          if constexpr (Cfg::kPtTmem) {
+            // key row r, queries [64 half, 64 half + 64): columns [32 half, 32 half + 32)
+            tmem_st_32x32b_x32(lb + Cfg::kPTT + half * 32, hp);
+          }
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
             const uint32_t off = (uint32_t)((ch ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(pt_row + off) =
-                make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
+            if constexpr (!Cfg::kPtTmem)
+              *reinterpret_cast<uint4*>(pt_row + off) =
+                  make_uint4(hp[ch * 4], hp[ch * 4 + 1], hp[ch * 4 + 2], hp[ch * 4 + 3]);
             *reinterpret_cast<uint4*>(dst_row + off) =
                 make_uint4(hd[ch * 4], hd[ch * 4 + 1], hd[ch * 4 + 2], hd[ch * 4 + 3]);
           }
+          if constexpr (Cfg::kPtTmem) {
+            tmem_wait_st();
+            tc_fence_before();
+          }
           fence_proxy_async_smem();
           mbar_arrive(p_full);
+          if (tracer) BWD_TRACE(kTrPFull, t);
         }
       }
-      // one dQ buffer: read it now; two: read the previous block's while this
-      // block's dQ product runs
-      if (Cfg::kDQBufs == 1) readout(t);
-      else if (t > 0) readout(t - 1);
     }
-    if (Cfg::kDQBufs == 2 && steps > 0) readout(steps - 1);
-    if (leader) bulk_wait_group0();
     // the last dV / dK products have retired
     if (ok && steps > 0 &&
         !mbar_wait_warp(pt_free, (uint32_t)(steps - 1) & 1u, a.status, kErrWaitTimeoutAccum, 324))
       ok = false;
+    if (tracer) BWD_TRACE(kTrEpiStart, 0);
     // dK (scaled) and dV: key row r, this warpgroup's half of the columns.
     // `ok` is warp-uniform (mbar_wait_warp); the TMEM loads are warp-collective
     // and run in every lane, only the stores depend on the key being in range.
@@ -469,6 +480,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (tracer) BWD_TRACE(kTrEpiEnd, 0);
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ dQ read-out
+    // dQ_t: TMEM -> registers -> swizzled fp32 box -> TMA reduce-add into the
+    // fp32 accumulator.  Rows past T add zeros (P is 0 there).  With two boxes
+    // chunks of 32 columns alternate, so staging chunk c only waits for the
+    // reduction issued two chunks earlier; with one box, for the previous.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the block
+    const uint32_t lb = tmem + ((uint32_t)(quarter * 32) << 16);
+    const bool leader = warp == 12 && lane == 0;  // issues the TMA reductions
+    bool ok = true;
+    int chunk = 0;
+    for (int tt = 0; tt < steps; ++tt) {
+      const int q0 = (i_start + tt) * BQ;
+      const int bi = tt % Cfg::kDQBufs;
+      const uint32_t buf = (uint32_t)(bi * D);
+      if (ok && !mbar_wait_warp(&dq_full[bi], (uint32_t)(tt / Cfg::kDQBufs) & 1u, a.status, kErrWaitTimeoutAccum, 322))
+        ok = false;
+      if (leader) BWD_TRACE(kTrDqFull, tt);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c, ++chunk) {
+        uint32_t v[32];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld_32x32b_x32_async(lb + Cfg::kDQ + buf + c * 32, v);
+          tmem_wait_ld_regs<32>(v);
+          if (c == D / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&dq_free[bi]);  // this dQ buffer may be overwritten
+          }
+        }
+        uint8_t* box = sStage + (Cfg::kStageBoxes == 2 ? (chunk & 1) : 0) * Cfg::kStage;
+        if (leader) {  // the reduction that last used this box has read it
+          if constexpr (Cfg::kStageBoxes == 2)
+            bulk_wait_group_read1();
+          else
+            bulk_wait_group_read0();
+        }
+        named_barrier_sync(1, kReadout);
+        if (ok) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(box + r * 128 + ((ch ^ (r & 7)) << 4)) =
+                make_uint4(v[ch * 4], v[ch * 4 + 1], v[ch * 4 + 2], v[ch * 4 + 3]);
+          fence_proxy_async_smem();
+        }
+        named_barrier_sync(1, kReadout);
+        if (leader && ok) {
+          tma_reduce_add_2d(&tm_dq, box, h * D + c * 32, row0 + q0);
+          bulk_commit_group();
+        }
+      }
+      if (leader) BWD_TRACE(kTrDqDone, tt);
+    }
+    if (leader) bulk_wait_group0();
   }
 
   tc_fence_before();
@@ -512,6 +579,7 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   a.dq_accum = p.dq_accum;
   a.dqkv = p.dq;
   a.status = device_status_ptr();
+  a.trace = g_bwd_trace;
   dim3 grid((p.f.T + BK - 1) / BK, p.f.B * p.f.H);
   fa_bwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tq, td, tdq, a);
   note_launch();
@@ -531,6 +599,8 @@ bool flash_attn_bwd_tc_supported(const AttnBwdParams& p) {
   return (p.f.D == 64 || p.f.D == 128) && fused_in && fused_out && dout_ok &&
          (reinterpret_cast<uintptr_t>(p.f.q) & 15u) == 0;
 }
+
+void set_attn_bwd_trace(unsigned long long* buf) { g_bwd_trace = buf; }
 
 void flash_attn_bwd_tc_main(const AttnBwdParams& p, cudaStream_t s) {
   if (p.f.D == 64) launch_bwd<64>(p, s);
