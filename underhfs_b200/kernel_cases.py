@@ -1,13 +1,16 @@
 """Single-kernel workloads for profiling and micro-benchmarking.
 
     python -m underhfs_b200.kernel_cases <case> [--iters N] [--time]
+    python -m underhfs_b200.kernel_cases attn_bwd --trace
 
 Each case builds its inputs once, launches one native kernel (or one fused
 op) ``--iters`` times and checks the device status word.  Sizes are chosen
 so the operands are larger than the 126 MB L2 where the kernel is
 memory-bound, while the whole case stays at a few GB of device memory, which
 keeps an ``ncu --set full`` capture of one launch short.  ``--time`` prints
-the CUDA-event time per launch after three warm-up launches.
+the CUDA-event time per launch after three warm-up launches.  ``--trace``
+(attn_bwd) prints the per-step clock stamps of the attention backward kernel
+for three key blocks of the first head (SM cycles from the CTA's start).
 
 Shapes follow the 125M TransformerLM step (16 x 1024 tokens, d_model 768,
 12 heads of 64, MLP 3072, vocab 32000) unless the case says otherwise.
@@ -171,13 +174,55 @@ def time_case(fn: Callable[[], object], iters: int = 20) -> float:
     return a.elapsed_time(b) / iters
 
 
+TRACE_EVENTS = ["start", "qdEmpty", "qdStored", "mmaS", "mmaGrads", "sFull", "sRegs", "math", "pFull", "dqFull",
+                "dqDone", "epiStart", "epiEnd", "kvFull"]
+
+
+def trace_attn_bwd(blocks=(0, 3, 6)) -> str:
+    """Run the attention backward of the 125M step (16 x 1024 tokens) once with clock stamps."""
+    qkv, o, lse, (B, T, H, D) = _attn_inputs(B=16)
+    do = _bf(B * T, H * D)
+    nblk = (T + 127) // 128
+    buf = torch.zeros(nblk * 16 * 64, dtype=torch.int64, device="cuda")
+    for _ in range(3):
+        K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, True)
+    torch.cuda.synchronize()
+    K.core().set_attn_bwd_trace(buf.data_ptr())
+    try:
+        K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, True)
+        torch.cuda.synchronize()
+    finally:
+        K.core().set_attn_bwd_trace(0)
+    tr = buf.view(nblk, 16, 64).cpu()
+    out = []
+    for blk in blocks:
+        if blk >= nblk:
+            continue
+        t0 = int(tr[blk, 0, 0])
+        steps = nblk - blk
+        out.append(f"key block {blk}: {steps} query steps; kvFull {int(tr[blk, 13, 0]) - t0}, "
+                   f"epiStart {int(tr[blk, 11, 0]) - t0}, epiEnd {int(tr[blk, 12, 0]) - t0}")
+        out.append("  step " + " ".join(f"{n:>8s}" for n in TRACE_EVENTS[1:11]))
+        for t in range(min(steps, 64)):
+            out.append(f"  {t:4d} " + " ".join(f"{int(tr[blk, e, t]) - t0:8d}" for e in range(1, 11)))
+    return "\n".join(out)
+
+
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", choices=sorted(CASES) + ["all"])
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="print CUDA-event time per launch")
+    ap.add_argument("--trace", action="store_true", help="attn_bwd: print the kernel's per-step clock stamps")
     args = ap.parse_args(argv)
     torch.manual_seed(0)
+    if args.trace:
+        if args.case != "attn_bwd":
+            ap.error("--trace is available for attn_bwd")
+        print(trace_attn_bwd())
+        st = K.core().device_status(True)
+        print("ok" if st["code"] == 0 else f"device status {st}")
+        return 0 if st["code"] == 0 else 1
     names = sorted(CASES) if args.case == "all" else [args.case]
     for name in names:
         fn, flops, nbytes = CASES[name]()
