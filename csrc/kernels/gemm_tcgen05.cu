@@ -1102,14 +1102,16 @@ bool pair_enabled() {
   return on;
 }
 
-// Measured on B200 (16384-row Linear layers, K = 768..3072): the pair kernel
-// wins for plain bf16 / fp32 outputs at every K and for the residual / GELU /
-// dGELU epilogues once K >= 2048; with a short main loop those epilogues
-// (row-wise aux loads, two output tiles) bound the tile and the single-CTA
-// kernel's smaller tiles balance better.
+// Measured on B200 (16384-row Linear layers, K = 768..3072, CUDA events):
+// the pair kernel wins for bf16 / fp32 outputs at every K, for bias + GELU
+// (78 vs 84 us at K = 768) and for the residual / dGELU epilogues once
+// K >= 2048 (64 vs 70 us); with a short main loop the row-wise aux loads of
+// the residual / dGELU epilogues bound the tile and the single-CTA kernel is
+// 4-7 % faster.
 bool pair_preferred(const GemmProblem& p) {
   if (!pair_enabled()) return false;
-  return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.epi == GEMM_EPI_F32_ACCUM || p.K >= 2048;
+  return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.epi == GEMM_EPI_F32_ACCUM ||
+         p.epi == GEMM_EPI_BIAS_GELU || p.K >= 2048;
 }
 }  // namespace
 
