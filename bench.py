@@ -46,7 +46,7 @@ CONFIGS = {
     "125m-ddp": dict(model="125m", batch=16, seq=1024, zero=0, desc=MODEL),
     "1.3b-zero2": dict(model="1.3b", batch=8, seq=2048, zero=2,
                        desc="1.3B TransformerLM (d_model 2048, 24 layers, 16 heads, MLP 8192, vocab 32000, tied)"),
-    "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3,
+    "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3, offload=True,
                      desc="7B TransformerLM (d_model 4096, 32 layers, 32 heads, MLP 11008, vocab 32000, untied)"),
 }
 
@@ -238,8 +238,9 @@ def run_zero3(args, pol, cc) -> int:
     if n > 1:
         init_process_group(pol)
     spec = PRESETS[cc["model"]]
+    offload = cc.get("offload", False) and not args.no_offload
     z = Zero3LM(spec, rank=pol.rank, world=n, device=f"cuda:{local}", lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
-                weight_decay=0.1, decoupled=True, seed=1234)
+                weight_decay=0.1, decoupled=True, seed=1234, offload_moments=offload)
     gen = torch.Generator().manual_seed(1234 + pol.rank)
     pool = [torch.randint(0, spec.vocab_size, (2, cc["batch"], cc["seq"]), generator=gen).cuda() for _ in range(2)]
 
@@ -296,7 +297,8 @@ def run_zero3(args, pol, cc) -> int:
             "data": "synthetic uniform token ids in [0,32000) from a fixed seed; random-init weights",
             "config": {"model": cc["desc"], "global_batch": n * cc["batch"], "micro_batch_per_gpu": cc["batch"],
                        "seq_len": cc["seq"], "parallelism": f"zero3-{n}",
-                       "optimizer": "ZeRO-3 AdamW: per-unit reduce-scatter fused with AdamW on owned rows",
+                       "optimizer": "ZeRO-3 AdamW: per-unit reduce-scatter fused with AdamW on owned rows"
+                                    + ("; Adam moments in pinned host RAM, staged per unit" if offload else ""),
                        "param_gather": "per-unit push all-gather over NVLink, prefetched one unit ahead",
                        "cuda_graph": False,
                        "l2": "no flush: per-step working set >> 126 MB L2"},
@@ -320,6 +322,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-offload", action="store_true",
+                    help="7b-zero3: keep the Adam moments on the device instead of pinned host RAM")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="125m-ddp",
                     help="125m-ddp is the headline run; the sharded configurations are measured the same way")
     args = ap.parse_args()

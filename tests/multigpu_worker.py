@@ -137,7 +137,8 @@ def case_zero3(rank: int, world: int) -> None:
     from underhfs_b200.parallel.zero3 import Zero3LM
 
     kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
-    for tied, fused in ((True, True), (False, True), (True, False)):
+    for tied, fused, offload in ((True, True, False), (False, True, False), (True, False, False),
+                                 (False, True, True)):
         cpu = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=3, heads=4,
                             tied=tied, init="normal", seed=3)
         state = {n: p._data.detach().float().clone() for n, p in cpu.named_parameters()}
@@ -145,8 +146,9 @@ def case_zero3(rank: int, world: int) -> None:
                             tied=tied, init="normal", seed=3)
         ref.to(f"cuda:{torch.cuda.current_device()}", dtype="bf16")
         ref_opt = FusedAdamW(ref.parameters(), **kw)
-        z = Zero3LM(cpu.spec, rank=rank, world=world, state=state, blocks=16, fused_gather=fused, **kw)
-        assert z.fused == fused
+        z = Zero3LM(cpu.spec, rank=rank, world=world, state=state, blocks=16, fused_gather=fused,
+                    offload_moments=offload, **kw)
+        assert z.fused == fused and z.offload == offload and (z.m.device.type == "cpu") == offload
         gen = torch.Generator().manual_seed(300 + rank)
         for _ in range(3):
             ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
@@ -170,7 +172,7 @@ def case_zero3(rank: int, world: int) -> None:
             # floor the scale: k_proj.bias has an exactly-zero gradient (a per-row
             # shift of the scores) and stays at rounding-noise size
             err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-3)).item()
-            assert err < 2e-2, (tied, fused, name, err)
+            assert err < 2e-2, (tied, fused, offload, name, err)
         z.close()
 
 

@@ -47,3 +47,15 @@ def test_rows_must_split_evenly():
     spec = LMSpec(1000, 256, 256, 1024, 1, heads=4, tied=True)  # 1000 rows / 16 ranks
     with pytest.raises(ValueError):
         _units(spec, 0, 16)
+
+
+def test_zero3_engine_has_every_engine_hook():
+    """Zero3Engine builds its own state instead of calling LMEngine.__init__;
+    every optional hook the shared forward/backward reads must still exist."""
+    from underhfs_b200.models.transformer import LMEngine
+    from underhfs_b200.parallel.zero3 import Zero3Engine
+
+    eng = Zero3Engine.__new__(Zero3Engine)
+    for name in ("context_attention", "positions"):
+        assert hasattr(eng, name) and getattr(eng, name) is None
+    assert issubclass(Zero3Engine, LMEngine)

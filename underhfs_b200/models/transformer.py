@@ -152,6 +152,12 @@ def initial_value(spec: LMSpec, name: str, shape: tuple[int, ...], init: str, ge
 class LMEngine:
     """Forward/backward of one TransformerLM over flat buffers, on the current stream."""
 
+    # context parallelism (parallel/context.py): attention over the group's
+    # sequence shards and the global positions of this rank's tokens; class
+    # defaults so engines that build their own state (ZeRO-3) inherit them
+    context_attention = None
+    positions: torch.Tensor | None = None
+
     def __init__(self, spec: LMSpec, flat: FlatBuffers, *, causal: bool = True) -> None:
         if spec.features % spec.heads != 0:
             raise ValueError("features must be divisible by heads")
@@ -161,10 +167,6 @@ class LMEngine:
         self.flat = flat
         self.causal = causal
         self.grad_ready: Callable[[int, int], None] | None = None
-        # context parallelism (parallel/context.py): attention over the group's
-        # sequence shards and the global positions of this rank's tokens
-        self.context_attention = None
-        self.positions: torch.Tensor | None = None
         self._saved: dict | None = None
         F = spec.features
         self.blocks = []

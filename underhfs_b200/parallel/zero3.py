@@ -23,6 +23,15 @@ The two slots of the block ring are reused every second block; the gather
 and reduce kernels open and close with a cross-rank barrier, so no rank
 overwrites a slot a peer is still reading.
 
+Moment offload (``offload_moments=True``): the fp32 Adam moments of the shard
+live in pinned host RAM.  A unit's moments (a contiguous shard range) are
+copied into one of two device staging slots on a copy stream when the unit's
+backward begins, the fused reduce-scatter + AdamW kernel updates them there,
+and they are copied back right after it (on a second copy stream: the two
+directions overlap), so the PCIe transfers overlap the backward of the
+neighbouring units.  Device memory for the moments drops
+from the whole shard to two units.
+
 The reference has no ZeRO-3 (its ZeroAwareAdamW is a single-process stub,
 optim.py:216-225).
 """
@@ -131,9 +140,10 @@ class Zero3LM:
                  group=None, init: str = "normal", seed: int = 0, state: dict | None = None,
                  lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, decoupled: bool = True, blocks: int = 128,
-                 overlap: bool = True, fused_gather: bool = True) -> None:
+                 overlap: bool = True, fused_gather: bool = True, offload_moments: bool = False) -> None:
         self.spec = spec
         self.overlap = overlap
+        self.offload = offload_moments
         self.fused = fused_gather
         self.rank, self.world = rank, world
         self.device = torch.device(device)
@@ -148,8 +158,21 @@ class Zero3LM:
         n = self.shard_total
         self.shard16 = torch.zeros(n, dtype=torch.bfloat16, device=self.device)
         self.master = torch.zeros(n, dtype=torch.float32, device=self.device)
-        self.m = torch.zeros_like(self.master)
-        self.v = torch.zeros_like(self.master)
+        if self.offload:
+            # moments in pinned host RAM, two device staging slots of [m | v] for the largest unit
+            self.m = torch.zeros(n, dtype=torch.float32, pin_memory=True)
+            self.v = torch.zeros(n, dtype=torch.float32, pin_memory=True)
+            umax = _round_up(max(u.shard_len for u in self.units.values()), 64)
+            self.stage = [torch.zeros(2, umax, dtype=torch.float32, device=self.device) for _ in range(2)]
+            # host -> device and device -> host on separate streams: PCIe is full duplex
+            self._copy = torch.cuda.Stream(device=self.device)
+            self._copy_back = torch.cuda.Stream(device=self.device)
+            self._staged: dict = {}       # unit key -> (slot, event: moments are on the device)
+            self._slot_free = [None, None]  # event: the slot's moments are back in host RAM
+            self._next_slot = 0
+        else:
+            self.m = torch.zeros_like(self.master)
+            self.v = torch.zeros_like(self.master)
         self.step_t = torch.zeros((), dtype=torch.int32, device=self.device)
         self._init_shards(init, seed, state)
         # gather / gradient slots: embed, tail, two ring slots for blocks
@@ -405,8 +428,54 @@ class Zero3LM:
     def _segs(self, u: _Unit):
         return [list(sg) for sg in u.segs]
 
+    # ------------------------------------------------------------ moment offload
+    def _stage_moments(self, key) -> None:
+        """Copy unit `key`'s moments host -> device staging slot (copy stream)."""
+        if key in self._staged:
+            return
+        u = self.units[key]
+        slot = self._next_slot
+        self._next_slot ^= 1
+        cs = self._copy
+        if self._slot_free[slot] is not None:
+            cs.wait_event(self._slot_free[slot])  # its previous unit's moments are back on the host
+        lo, ln = u.shard_lo, u.shard_len
+        with torch.cuda.stream(cs):
+            self.stage[slot][0, :ln].copy_(self.m[lo: lo + ln], non_blocking=True)
+            self.stage[slot][1, :ln].copy_(self.v[lo: lo + ln], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        self._staged[key] = (slot, ev)
+
+    def _moment_ptrs(self, key, stream: torch.cuda.Stream) -> tuple[int, int, int]:
+        """(m, v) base pointers for the update kernel: shard offsets of this unit
+        land in its staging slot."""
+        self._stage_moments(key)
+        slot, ev = self._staged[key]
+        stream.wait_event(ev)
+        lo = self.units[key].shard_lo
+        return slot, self.stage[slot][0].data_ptr() - lo * 4, self.stage[slot][1].data_ptr() - lo * 4
+
+    def _unstage_moments(self, key, slot: int, stream: torch.cuda.Stream) -> None:
+        """After the update on `stream`: copy the unit's moments back to host RAM."""
+        u = self.units[key]
+        done = torch.cuda.Event()
+        done.record(stream)
+        cs = self._copy_back
+        cs.wait_event(done)
+        lo, ln = u.shard_lo, u.shard_len
+        with torch.cuda.stream(cs):
+            self.m[lo: lo + ln].copy_(self.stage[slot][0, :ln], non_blocking=True)
+            self.v[lo: lo + ln].copy_(self.stage[slot][1, :ln], non_blocking=True)
+        back = torch.cuda.Event()
+        back.record(cs)
+        self._slot_free[slot] = back
+        del self._staged[key]
+
     def backward_begin(self, key) -> None:
         cur = torch.cuda.current_stream()
+        if self.offload:
+            self._stage_moments(key)
         if key == "tail":
             K.increment_(self.step_t)
             # the head gradient of a tied model lands in the embedding unit
@@ -437,14 +506,21 @@ class Zero3LM:
         if self.overlap:
             comm = self._comm()
             comm.wait_stream(torch.cuda.current_stream())
-            stream = comm.cuda_stream
+            run = comm
         else:
-            stream = self.stream()
+            run = torch.cuda.current_stream()
+        stream = run.cuda_stream
+        if self.offload:
+            mslot, m_ptr, v_ptr = self._moment_ptrs(key, run)
+        else:
+            m_ptr, v_ptr = self.m.data_ptr(), self.v.data_ptr()
         core().comm_rs_adamw_segments(
-            self.gradsym.heap, self.slot_off[slot] * 4, self._segs(u), self.master.data_ptr(), self.m.data_ptr(),
-            self.v.data_ptr(), self.shard16.data_ptr(), float(self.lr), float(self.betas[0]), float(self.betas[1]),
+            self.gradsym.heap, self.slot_off[slot] * 4, self._segs(u), self.master.data_ptr(), m_ptr,
+            v_ptr, self.shard16.data_ptr(), float(self.lr), float(self.betas[0]), float(self.betas[1]),
             float(self.eps), float(self.weight_decay), float(1.0 / self.world), bool(self.decoupled),
             self.step_t.data_ptr(), self.nblocks, stream)
+        if self.offload:
+            self._unstage_moments(key, mslot, run)
         if self.overlap:
             ev = torch.cuda.Event()
             ev.record(self._comm())
