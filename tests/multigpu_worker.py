@@ -222,6 +222,20 @@ def case_cp(rank: int, world: int) -> None:
     lerr = abs(lsum.item() / world - ref_loss.item()) / abs(ref_loss.item())
     gerr = ((g - ref).abs().max() / ref.abs().max()).item()
     assert lerr < 2e-3 and gerr < 3e-2, (lerr, gerr)
+    # the same through the public trainer: full sequences in, sharded per rank
+    from underhfs_b200.distributed import policy_from_env
+    from underhfs_b200.train import TrainConfig, Trainer
+
+    cfg = TrainConfig(model="125m", batch=2, seq_len=T, context_parallel=True, cuda_graph=True)
+    tmodel = _model(max_seq_len=T)
+    trainer = Trainer(tmodel, cfg, policy=policy_from_env())
+    assert trainer.cp is not None and not cfg.cuda_graph
+    host = torch.stack([ids, tg]).cpu().pin_memory()
+    first = trainer.step_from_host(host)
+    for _ in range(3):
+        last = trainer.step_from_host(host)
+    assert last < first, (first, last)
+    trainer.release()
     from underhfs_b200.ops._lib import core
 
     assert core().device_status(True)["code"] == 0

@@ -29,8 +29,12 @@ def _heartbeat_worker(rank, world, port, scenario, q):
     sys.path.insert(0, str(ROOT))
     from underhfs_b200.parallel.elastic import Heartbeat, PeerFailure, make_store
 
-    store = make_store(rank, world, port=port, timeout_s=10.0)
-    hb = Heartbeat(store, rank, world, deadline_s=1.0, interval_s=0.05)
+    store = make_store(rank, world, port=port, timeout_s=30.0)
+    # start together: process start-up (spawn + imports) can differ by seconds
+    # under load, which must not read as a rank that never joined
+    store.set(f"up/{rank}", "1")
+    store.wait([f"up/{r}" for r in range(world)])
+    hb = Heartbeat(store, rank, world, deadline_s=1.0, interval_s=0.05, grace_s=20.0)
     try:
         for step in range(200):
             hb.beat(step)

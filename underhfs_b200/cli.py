@@ -121,7 +121,8 @@ def _cmd_train(args) -> int:
     from underhfs_b200.train import TrainConfig, Trainer, build_model
 
     cfg = TrainConfig(model=args.model, batch=args.batch, seq_len=args.seq_len_train, lr=args.lr_train,
-                      zero_stage=args.zero, cuda_graph=not args.no_graph)
+                      zero_stage=args.zero, cuda_graph=not args.no_graph,
+                      context_parallel=getattr(args, "context_parallel", False))
     from underhfs_b200.distributed import policy_from_env
 
     pol = policy_from_env(zero_stage=cfg.zero_stage)
@@ -129,7 +130,9 @@ def _cmd_train(args) -> int:
         torch.cuda.set_device(pol.local_rank or 0)
     model = build_model(cfg, device=f"cuda:{pol.local_rank or 0}")
     trainer = Trainer(model, cfg, policy=pol)
-    data = SyntheticTokens(model.vocab_size, cfg.batch, cfg.seq_len, seed=cfg.seed, rank=pol.rank)
+    # context parallelism: every rank draws the same sequences and trains on its shard
+    data = SyntheticTokens(model.vocab_size, cfg.batch, cfg.seq_len, seed=cfg.seed,
+                           rank=0 if cfg.context_parallel else pol.rank)
     host = torch.empty((2, cfg.batch, cfg.seq_len), dtype=torch.int64, pin_memory=True)
     losses = []
     for _ in range(args.steps):
@@ -277,6 +280,8 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--lr-train", type=float, default=3e-4)
     p.add_argument("--zero", type=int, default=0)
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--context-parallel", action="store_true",
+                   help="shard every sequence over all ranks (zigzag) instead of giving each rank its own batch")
     p.set_defaults(func=_cmd_train)
 
     p = sub.add_parser("checkpoint")

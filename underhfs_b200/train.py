@@ -43,6 +43,9 @@ class TrainConfig:
     cuda_graph: bool = True
     seed: int = 0
     init: str = "normal"
+    # every rank trains on its zigzag shard of the same sequences (the whole
+    # world is one context-parallel group; gradients are averaged by DDP)
+    context_parallel: bool = False
 
 
 def build_model(cfg: TrainConfig, device: str = "cuda"):
@@ -68,6 +71,16 @@ class Trainer:
         self.ddp = None
         if self.world > 1 and cfg.zero_stage == 0:
             self.ddp = DistributedDataParallel(model, self.policy, bucket_mb=cfg.bucket_mb)
+        self.cp = None
+        if cfg.context_parallel:
+            if self.world < 2 or cfg.zero_stage != 0:
+                raise ValueError("context_parallel needs world_size > 1 and data-parallel (zero_stage 0) gradients")
+            from underhfs_b200.parallel.context import enable_context_parallel
+
+            self.cp = enable_context_parallel(model.engine, cfg.seq_len)
+            # the attention's K/V all-gather / dK-dV reduce-scatter run as
+            # NCCL collectives from Python; the step stays eager
+            cfg.cuda_graph = False
         if cfg.zero_stage > 0:
             if self.world > 1:
                 from underhfs_b200.distributed import init_process_group
@@ -80,9 +93,12 @@ class Trainer:
             self.opt = FusedAdamW(model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                   weight_decay=cfg.weight_decay, decoupled=cfg.decoupled)
         dev = model.flat.device
-        self.static_ids = torch.zeros((cfg.batch, cfg.seq_len), dtype=torch.int64, device=dev)
+        local_len = cfg.seq_len // self.world if self.cp is not None else cfg.seq_len
+        self.static_ids = torch.zeros((cfg.batch, local_len), dtype=torch.int64, device=dev)
         self.static_tg = torch.zeros_like(self.static_ids)
-        self.static_batch = torch.zeros((2, cfg.batch, cfg.seq_len), dtype=torch.int64, device=dev)
+        self.static_batch = torch.zeros((2, cfg.batch, local_len), dtype=torch.int64, device=dev)
+        self._full_batch = (torch.zeros((2, cfg.batch, cfg.seq_len), dtype=torch.int64, device=dev)
+                            if self.cp is not None else None)
         self._graph = None
         self._graph_loss = None
         self.steps_done = 0
@@ -144,9 +160,25 @@ class Trainer:
         self._graph.replay()
         return self._graph_loss
 
+    def local_batch(self, ids: torch.Tensor, targets: torch.Tensor):
+        """This rank's part of full-sequence ids / targets [B, T] (the identity
+        without context parallelism)."""
+        if self.cp is None:
+            return ids, targets
+        from underhfs_b200.parallel.context import shard_sequence
+
+        return (shard_sequence(ids, self.cp.rank, self.cp.size), shard_sequence(targets, self.cp.rank, self.cp.size))
+
     def step_from_host(self, host_batch: torch.Tensor) -> float:
-        """End-to-end step: pinned host [2, B, T] int64 batch in, host float loss out."""
-        self.static_batch.copy_(host_batch, non_blocking=True)
+        """End-to-end step: pinned host [2, B, T] int64 batch in, host float loss out.
+        With context parallelism every rank passes the same full sequences."""
+        if self.cp is not None:
+            self._full_batch.copy_(host_batch, non_blocking=True)
+            ids, tg = self.local_batch(self._full_batch[0], self._full_batch[1])
+            self.static_batch[0].copy_(ids)
+            self.static_batch[1].copy_(tg)
+        else:
+            self.static_batch.copy_(host_batch, non_blocking=True)
         loss = self.step(self.static_batch[0], self.static_batch[1])
         return float(loss.item())
 
