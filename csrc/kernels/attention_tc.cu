@@ -69,6 +69,16 @@ struct FwdCfg {
   static constexpr uint32_t kTmemCols = 512;
 };
 
+// Optional per-block clock stamps (clock64) for the CTAs of head 0 of batch 0:
+// trace[(cta * kTraceEvents + event) * kTraceSteps + block], cta = blockIdx.x.
+// Off (nullptr) unless a buffer is installed with set_attn_fwd_trace.
+constexpr int kTraceEvents = 16, kTraceSteps = 64;
+enum FwdTraceEvent {
+  kTrStart = 0, kTrQFull, kTrKFull, kTrIssueS, kTrIssuePv, kTrSFullA, kTrSRegsA, kTrExpA, kTrODoneA, kTrPFullA,
+  kTrSFullB, kTrPFullB, kTrEpiStart, kTrEpiEnd
+};
+unsigned long long* g_fwd_trace = nullptr;
+
 struct FwdArgs {
   int H, T;
   long long F;            // H * D (columns per q / k / v section)
@@ -78,7 +88,14 @@ struct FwdArgs {
   long long o_stride_t;   // elements between tokens of o (rows are [b*T + t])
   float* lse;             // [B, H, T] (log2 domain)
   DeviceStatus* status;
+  unsigned long long* trace;
 };
+
+#define FWD_TRACE(ev, step)                                                                              \
+  do {                                                                                                   \
+    if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
+      a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
+  } while (0)
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -216,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       bool ok = mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 210);
+      FWD_TRACE(kTrQFull, 0);
       // S of block j for both tiles goes ahead of PV of block j-1: a softmax
       // warpgroup frees S as soon as it holds the row in registers, so the
       // next S is ready when it finishes P, and the PV product overlaps the
@@ -225,17 +243,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        FWD_TRACE(kTrKFull, j);
         if ((j < nA && !issue_s(0, j)) || !issue_s(1, j)) {
           ok = false;
           break;
         }
         tc_commit(&slot_empty[slot_of(2 * j)]);  // K_j read by both tiles
+        FWD_TRACE(kTrIssueS, j);
         if (j >= 1) {
           if ((j - 1 < nA && !issue_pv(0, j - 1)) || !issue_pv(1, j - 1)) {
             ok = false;
             break;
           }
           tc_commit(&slot_empty[slot_of(2 * (j - 1) + 1)]);  // V_{j-1} read by both tiles
+          FWD_TRACE(kTrIssuePv, j - 1);
         }
       }
       if (ok && nB > 0) {
@@ -260,11 +281,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int key_limit = a.causal ? min(q + 1, T) : T;  // keys [0, key_limit) are visible
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    const bool tracer = quarter == 0 && lane == 0;  // warp 0 (tile A) and warp 4 (tile B)
+    if (tracer && t == 0) FWD_TRACE(kTrStart, 0);
     for (int j = 0; j < nblk && ok; ++j) {
       if (!mbar_wait_warp(&s_full[t], (uint32_t)j & 1u, a.status, kErrWaitTimeoutAccum, 220)) {
         ok = false;
         break;
       }
+      if (tracer) FWD_TRACE(t == 0 ? kTrSFullA : kTrSFullB, j);
       tc_fence_after();
       uint32_t sr[BKV];
 #pragma unroll
@@ -272,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld_regs<BKV>(sr);
       tc_fence_before();
       mbar_arrive(&s_free[t]);  // S_t may be overwritten by the next block
+      if (tracer && t == 0) FWD_TRACE(kTrSRegsA, j);
       const int lim = key_limit - j * BKV;  // visible columns of this block: [0, lim)
       if (lim < BKV) {
 #pragma unroll
@@ -302,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m_run = m_new;
+      if (tracer && t == 0) FWD_TRACE(kTrExpA, j);
       // PV(j-1) finished: the P tile is free and O_t holds blocks < j
       if (j > 0) {
         if (!mbar_wait_warp(&o_done[t], (uint32_t)(j - 1) & 1u, a.status, kErrWaitTimeoutAccum, 221)) {
@@ -309,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        if (tracer && t == 0) FWD_TRACE(kTrODoneA, j);
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
@@ -332,10 +359,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();  // P stores visible to the tensor core
       tc_fence_before();         // O rescale stores ordered before the next MMA
       mbar_arrive(&p_full[t]);
+      if (tracer) FWD_TRACE(t == 0 ? kTrPFullA : kTrPFullB, j);
     }
     if (ok && nblk > 0)
       ok = mbar_wait_warp(&o_done[t], (uint32_t)(nblk - 1) & 1u, a.status, kErrWaitTimeoutAccum, 222);
     // epilogue: O / l and LSE (TMEM loads in every lane, stores for rows < T)
+    if (tracer && t == 0) FWD_TRACE(kTrEpiStart, 0);
     if (ok) {
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
@@ -359,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (q < T) a.lse[(long long)bh * T + q] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
     }
+    if (tracer && t == 0) FWD_TRACE(kTrEpiEnd, 0);
   }
 
   tc_fence_before();
@@ -397,6 +427,7 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
   a.o_stride_t = p.o_stride_t;
   a.lse = p.lse;
   a.status = device_status_ptr();
+  a.trace = g_fwd_trace;
   dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
   fa_fwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();
@@ -413,6 +444,8 @@ bool flash_attn_fwd_tc_supported(const AttnParams& p) {
          p.o_stride_b == (long long)p.T * p.o_stride_t && (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0 &&
          (reinterpret_cast<uintptr_t>(p.o) & 15u) == 0 && (p.o_stride_t % 8) == 0;
 }
+
+void set_attn_fwd_trace(unsigned long long* buf) { g_fwd_trace = buf; }
 
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s) {
   if (p.D == 64) launch_fwd<64>(p, s);

@@ -376,9 +376,12 @@ void colsum_accum(const __nv_bfloat16* x, long long ld, float* out, int rows, in
   if (rows <= 0 || cols <= 0) return;
   if (cols % 8 == 0 && ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
     const int gx = (cols + 255) / 256;
-    // ~8 blocks (64 warps) per SM keep enough loads in flight, but at most 64
-    // blocks per column range so the per-column atomics do not serialise in L2
-    int gy = min(64, (8 * 148 + gx - 1) / gx);
+    // ~8 blocks (64 warps) per SM keep enough loads in flight.  Wide
+    // matrices cap the blocks per column range at 64 (the per-column atomics
+    // then stay off the critical path: 16384 x 3072 in 15.6 us); narrow ones
+    // (fewer than 8 column ranges) need up to 256 to fill the GPU at all
+    // (a cap of 64 gives 192 blocks, 1.3 waves, for 768 columns).
+    int gy = min(gx < 8 ? 256 : 64, (8 * 148 + gx - 1) / gx);
     int rpb = (rows + gy - 1) / gy;
     rpb = (rpb + 7) / 8 * 8;
     gy = (rows + rpb - 1) / rpb;

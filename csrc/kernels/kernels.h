@@ -110,6 +110,9 @@ void flash_attn_fwd(const AttnParams& p, cudaStream_t s);
 // Per-step clock stamps of the tcgen05 attention backward (head 0 of batch 0):
 // a buffer of ceil(T/128) * 16 * 64 uint64 values, or nullptr (off).
 void set_attn_bwd_trace(unsigned long long* buf);
+// Per-key-block clock stamps of the tcgen05 attention forward (head 0 of
+// batch 0): a buffer of ceil(T/256) * 16 * 64 uint64 values, or nullptr.
+void set_attn_fwd_trace(unsigned long long* buf);
 // tcgen05/TMEM forward for the fused-QKV layout (attention_tc.cu)
 bool flash_attn_fwd_tc_supported(const AttnParams& p);
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s);

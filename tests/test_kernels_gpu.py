@@ -142,6 +142,20 @@ def test_matmul_bf16_and_f32(K):
     assert exact.tolist() == [[19.0, 22.0], [43.0, 50.0]]
 
 
+@pytest.mark.parametrize("rows,cols", [(16384, 768), (16384, 3072), (300, 264), (1000, 130), (7, 8)])
+def test_bias_gradient_colsum(K, rows, cols):
+    """out[c] += sum_r x[r, c] (fp32 accumulate) against the fp32 oracle,
+    vectorised (cols % 8 == 0) and scalar paths, accumulating twice."""
+    x = bf(torch.randn(rows, cols, device="cuda"))
+    out = torch.zeros(cols, device="cuda")
+    K.colsum_accum(x, out)
+    ref = x.float().sum(0)
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3 * rows ** 0.5)
+    K.colsum_accum(x, out)
+    assert torch.allclose(out, 2 * ref, rtol=1e-4, atol=2e-3 * rows ** 0.5)
+    _status_ok()
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 def test_elementwise_reduce_cast(K, dtype):
     n = (1 << 20) + 7

@@ -1,7 +1,7 @@
 """Single-kernel workloads for profiling and micro-benchmarking.
 
     python -m underhfs_b200.kernel_cases <case> [--iters N] [--time]
-    python -m underhfs_b200.kernel_cases attn_bwd --trace
+    python -m underhfs_b200.kernel_cases {attn_fwd,attn_bwd} --trace
 
 Each case builds its inputs once, launches one native kernel (or one fused
 op) ``--iters`` times and checks the device status word.  Sizes are chosen
@@ -9,8 +9,8 @@ so the operands are larger than the 126 MB L2 where the kernel is
 memory-bound, while the whole case stays at a few GB of device memory, which
 keeps an ``ncu --set full`` capture of one launch short.  ``--time`` prints
 the CUDA-event time per launch after three warm-up launches.  ``--trace``
-(attn_bwd) prints the per-step clock stamps of the attention backward kernel
-for three key blocks of the first head (SM cycles from the CTA's start).
+(attn_fwd / attn_bwd) prints the per-block clock stamps of the attention
+kernel for a few CTAs of the first head (SM cycles from the CTA's start).
 
 Shapes follow the 125M TransformerLM step (16 x 1024 tokens, d_model 768,
 12 heads of 64, MLP 3072, vocab 32000) unless the case says otherwise.
@@ -208,6 +208,42 @@ def trace_attn_bwd(blocks=(0, 3, 6)) -> str:
     return "\n".join(out)
 
 
+FWD_TRACE_EVENTS = ["start", "qFull", "kFull", "issueS", "issuePV", "sFullA", "sRegsA", "expA", "oDoneA", "pFullA",
+                    "sFullB", "pFullB", "epiStart", "epiEnd"]
+
+
+def trace_attn_fwd(ctas=(0, 2)) -> str:
+    """Run the attention forward of the 125M step (16 x 1024 tokens) once with
+    per-key-block clock stamps (tile A = the CTA's first 128 queries)."""
+    qkv, _, _, (B, T, H, D) = _attn_inputs(B=16)
+    nct = (T + 255) // 256
+    buf = torch.zeros(nct * 16 * 64, dtype=torch.int64, device="cuda")
+    for _ in range(3):
+        K.flash_attn_qkv(qkv, B, T, H, D, True)
+    torch.cuda.synchronize()
+    K.core().set_attn_fwd_trace(buf.data_ptr())
+    try:
+        K.flash_attn_qkv(qkv, B, T, H, D, True)
+        torch.cuda.synchronize()
+    finally:
+        K.core().set_attn_fwd_trace(0)
+    tr = buf.view(nct, 16, 64).cpu()
+    out = []
+    for c in ctas:
+        if c >= nct:
+            continue
+        t0 = int(tr[c, 0, 0])
+        m_block = nct - 1 - c  # the kernel runs the longest rows first
+        n_b = min((T + 127) // 128, 2 * m_block + 2)
+        out.append(f"CTA {c} (queries {m_block * 256}..{m_block * 256 + 255}): {n_b} key blocks; "
+                   f"qFull {int(tr[c, 1, 0]) - t0}, epiStart {int(tr[c, 12, 0]) - t0}, epiEnd {int(tr[c, 13, 0]) - t0}")
+        out.append("  blk  " + " ".join(f"{n:>8s}" for n in FWD_TRACE_EVENTS[2:12]))
+        for j in range(n_b):
+            out.append(f"  {j:4d} " + " ".join(f"{int(tr[c, e, j]) - t0:8d}" if int(tr[c, e, j]) else f"{'-':>8s}"
+                                             for e in range(2, 12)))
+    return "\n".join(out)
+
+
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", choices=sorted(CASES) + ["all"])
@@ -217,9 +253,9 @@ def main(argv: list[str] | None = None) -> int:
     args = ap.parse_args(argv)
     torch.manual_seed(0)
     if args.trace:
-        if args.case != "attn_bwd":
-            ap.error("--trace is available for attn_bwd")
-        print(trace_attn_bwd())
+        if args.case not in ("attn_bwd", "attn_fwd"):
+            ap.error("--trace is available for attn_fwd and attn_bwd")
+        print(trace_attn_bwd() if args.case == "attn_bwd" else trace_attn_fwd())
         st = K.core().device_status(True)
         print("ok" if st["code"] == 0 else f"device status {st}")
         return 0 if st["code"] == 0 else 1
