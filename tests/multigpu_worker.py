@@ -82,6 +82,32 @@ def case_ddp(rank: int, world: int) -> None:
         torch.cuda.synchronize()
         err = ((model.flat.grads - ref).abs().max() / ref.abs().max()).item()
         assert err < 1e-4, err
+    # optimizer step split around the last (embedding) all-reduce: the same
+    # weights as one step after every reduction.  The weight-gradient GEMMs
+    # accumulate with fp32 atomics, so two runs differ in the last bits; eps
+    # 1e-3 keeps Adam from turning those into sign flips of near-zero updates.
+    from underhfs_b200.optim import FusedAdamW
+
+    outs = []
+    for split in (False, True):
+        m2 = _model()
+        d2 = DistributedDataParallel(m2, policy_from_env(), bucket_mb=0.25)
+        opt = FusedAdamW(m2.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
+        for _ in range(2):
+            m2.zero_grad()
+            d2(ids, tg).backward()
+            if split:
+                boundary = d2.synchronize_gradients(defer_tail=True)
+                assert boundary > 0  # the tied embedding is reduced last
+                opt.step_split(boundary, d2.wait_gradients)
+            else:
+                d2.synchronize_gradients()
+                opt.step()
+        torch.cuda.synchronize()
+        outs.append(m2.flat.master.clone())
+    moved = (outs[0] - _model().flat.master).abs().max().item()  # how far two steps moved the weights
+    diff = (outs[0] - outs[1]).abs().max().item()
+    assert diff < 1e-3 * moved, (diff, moved)
     with ddp.no_sync():
         model.zero_grad()
         ddp(ids, tg).backward()

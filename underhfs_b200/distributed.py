@@ -320,18 +320,21 @@ class DistributedDataParallel:
         with self.group.no_sync():
             yield
 
-    def synchronize_gradients(self) -> None:
+    def synchronize_gradients(self, defer_tail: bool = False) -> int:
+        """All-reduce (average) the gradients.  ``defer_tail=True`` (fused
+        engine only) returns the flat offset below which the last reduction is
+        still running (0: everything is final); call ``wait_gradients()``
+        before reading gradients below it."""
         if not self.group.synchronized:
-            return
+            return 0
         _require_collective(self.policy)
         if self.policy.world_size == 1:
-            return
+            return 0
         if self._bucketer is not None:
-            self._bucketer.finish()
-            return
+            return self._bucketer.finish(defer_tail=defer_tail)
         params = [p for p in self.module.parameters() if p.grad is not None]
         if not params:
-            return
+            return 0
         grads = [p.grad._data.detach() for p in params]
         dev = _coll_device(self.policy)
         flat = torch.cat([g.reshape(-1).to(dev, torch.float32) for g in grads])
@@ -343,6 +346,12 @@ class DistributedDataParallel:
             n = g.numel()
             p.grad = Tensor._wrap(flat[off : off + n].view(g.shape).to(g.device, g.dtype), like=p)
             off += n
+        return 0
+
+    def wait_gradients(self) -> None:
+        """Complete a ``synchronize_gradients(defer_tail=True)``."""
+        if self._bucketer is not None:
+            self._bucketer.wait_tail()
 
 
 DDP = DistributedDataParallel

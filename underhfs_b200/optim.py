@@ -21,7 +21,7 @@ reduce-scatter + AdamW + all-gather kernel over NVLink (parallel/zero.py).
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Iterable
+from typing import Callable, Iterable
 
 import torch
 
@@ -226,13 +226,33 @@ class AdamW(Optimizer):
             else:
                 self._cpu_step(i, p, g, b1, b2)
 
-    def _flat_step(self, b1: float, b2: float) -> None:
+    def _flat_step(self, b1: float, b2: float, lo: int = 0, hi: int | None = None, increment: bool = True) -> None:
         from underhfs_b200.ops import kernels as K
 
         f = self._flat
-        K.increment_(self._step_t)
-        K.adamw_(f.master, f.grads, self._m_flat, self._v_flat, f.params, lr=self.lr, beta1=b1, beta2=b2,
-                 eps=self.eps, weight_decay=self.weight_decay, decoupled=self.decoupled, step_t=self._step_t)
+        hi = f.master.numel() if hi is None else min(hi, f.master.numel())
+        if increment:
+            K.increment_(self._step_t)
+        if hi <= lo:
+            return
+        K.adamw_(f.master[lo:hi], f.grads[lo:hi], self._m_flat[lo:hi], self._v_flat[lo:hi], f.params[lo:hi],
+                 lr=self.lr, beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.weight_decay,
+                 decoupled=self.decoupled, step_t=self._step_t)
+
+    def step_split(self, boundary: int, wait: Callable[[], None]) -> None:
+        """One optimizer step in two launches for a flat-buffer model whose
+        gradients below `boundary` are still being reduced: the parameters at
+        or above it are updated first (overlapping that reduction), then
+        `wait()` orders the stream after it and the rest is updated."""
+        if self._flat is None:
+            wait()
+            self.step()
+            return
+        self.step_count += 1
+        b1, b2 = self.betas
+        self._flat_step(b1, b2, boundary, None, increment=True)
+        wait()
+        self._flat_step(b1, b2, 0, boundary, increment=False)
 
     def _cuda_step(self, i: int, p: Tensor, g: Tensor, b1: float, b2: float) -> None:
         from underhfs_b200.ops import kernels as K
@@ -277,6 +297,10 @@ class FusedAdamW(AdamW):
     def step(self) -> None:
         self.last_kernel_status = fused_adamw_kernel_status(self.params)
         super().step()
+
+    def step_split(self, boundary: int, wait) -> None:
+        self.last_kernel_status = fused_adamw_kernel_status(self.params)
+        super().step_split(boundary, wait)
 
 
 @dataclass
@@ -327,6 +351,13 @@ class ZeroAwareAdamW(AdamW):
         self.step_count += 1
         self._zero.step(lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.weight_decay,
                         decoupled=self.decoupled)
+
+    def step_split(self, boundary: int, wait) -> None:
+        if self._zero is None:
+            super().step_split(boundary, wait)
+            return
+        wait()  # the sharded update reduces every gradient itself
+        self.step()
 
     def state_dict(self) -> dict:
         if self._zero is None:

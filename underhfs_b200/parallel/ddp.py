@@ -46,6 +46,7 @@ class BucketedAllReduce:
         self.buckets = [(edges[i + 1], edges[i]) for i in range(len(edges) - 1)]  # descending ranges
         self.stream = torch.cuda.Stream(priority=-1)
         self._next = 0
+        self._last = None
         self._enabled = True
         self._launched_any = False
         model.engine.grad_ready = self.on_ready
@@ -59,6 +60,7 @@ class BucketedAllReduce:
 
     def arm(self, enabled: bool = True) -> None:
         self._next = 0
+        self._last = None
         self._enabled = enabled
         self._launched_any = False
         self.model.engine.grad_ready = self.on_ready if enabled else None
@@ -66,6 +68,10 @@ class BucketedAllReduce:
     def _launch(self, lo: int, hi: int) -> None:
         nvtx.push(f"allreduce/bucket[{lo},{hi})")
         compute = torch.cuda.current_stream()
+        # every reduction launched before this one is done at `pre`
+        pre = torch.cuda.Event()
+        pre.record(self.stream)
+        self._last = (hi, pre)
         ev = torch.cuda.Event()
         ev.record(compute)
         self.stream.wait_event(ev)
@@ -103,7 +109,12 @@ class BucketedAllReduce:
         if self._next > first:
             self._launch(self.buckets[self._next - 1][0], self.buckets[first][1])
 
-    def finish(self) -> None:
+    def finish(self, defer_tail: bool = False) -> int:
+        """Launch the remaining buckets and order the compute stream after the
+        reductions.  With ``defer_tail`` the compute stream only waits for the
+        buckets launched during the backward and the offset below which
+        gradients are still being reduced is returned (0 when nothing is
+        pending); ``wait_tail()`` completes the wait."""
         # the rest (the embeddings, final only after the last kernel of the
         # backward) in one launch: no per-bucket synchronisation in the tail
         if self._next < len(self.buckets):
@@ -112,6 +123,14 @@ class BucketedAllReduce:
         if self.trace:
             end = torch.cuda.Event(enable_timing=True)
             end.record(torch.cuda.current_stream())  # backward kernels done
+        last, self._last = self._last, None
+        if defer_tail and last is not None and not self.trace:
+            # the last launch (the embeddings, made final by the end of the
+            # backward) covers [.., boundary); everything above is reduced
+            boundary, pre = last
+            torch.cuda.current_stream().wait_event(pre)
+            self._next = 0
+            return boundary
         torch.cuda.current_stream().wait_stream(self.stream)
         self._next = 0
         if self.trace and self._trace_events:
@@ -126,3 +145,8 @@ class BucketedAllReduce:
                   f"launch lag {start_lag:.3f} ms, from first bucket to backward end {first.elapsed_time(end):.3f} ms, "
                   f"reduction tail after backward {tail:.3f} ms", flush=True)
             self._trace_events = []
+        return 0
+
+    def wait_tail(self) -> None:
+        """The compute stream waits for every reduction (after finish(defer_tail=True))."""
+        torch.cuda.current_stream().wait_stream(self.stream)

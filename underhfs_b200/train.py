@@ -108,9 +108,18 @@ class Trainer:
         runner = self.ddp if self.ddp is not None else self.model
         loss = runner(ids, tg)
         loss.backward()
-        if self.ddp is not None:
-            self.ddp.synchronize_gradients()
-        self.opt.step()
+        if self.ddp is not None and hasattr(self.opt, "step_split"):
+            # the embedding gradients are final last (tied head): update every
+            # other parameter while their all-reduce is still running
+            boundary = self.ddp.synchronize_gradients(defer_tail=True)
+            if boundary > 0:
+                self.opt.step_split(boundary, self.ddp.wait_gradients)
+            else:
+                self.opt.step()
+        else:
+            if self.ddp is not None:
+                self.ddp.synchronize_gradients()
+            self.opt.step()
         return loss._data if hasattr(loss, "_data") else loss
 
     def _state_tensors(self) -> list[torch.Tensor]:
