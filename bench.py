@@ -6,7 +6,11 @@ fp32 master weights, sequence 1024, micro-batch 16 per GPU (weak scaling),
 FusedAdamW lr 3e-4, gradients all-reduced in 25 MB buckets overlapped with
 backward.  Synthetic uniform token ids from a seed, random-init weights.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+
+``--config tiny-cpu`` runs the CPU-fallback configuration instead (50 AdamW
+steps of a d_model-64 model on 8 x 64 byte ids, checkpoint round trip,
+greedy generation), which the reference's own runtime can also complete.
 
 For N > 1 launch with torchrun (one rank per GPU); RANK / LOCAL_RANK /
 WORLD_SIZE / MASTER_* come from the environment.  Rank 0 prints one JSON line.
@@ -48,7 +52,115 @@ CONFIGS = {
                        desc="1.3B TransformerLM (d_model 2048, 24 layers, 16 heads, MLP 8192, vocab 32000, tied)"),
     "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3, offload=True,
                      desc="7B TransformerLM (d_model 4096, 32 layers, 32 heads, MLP 11008, vocab 32000, untied)"),
+    # the CPU-fallback configuration: the one the reference's own runtime can
+    # complete (pure Python, about 2.2-2.5 tokens/s on an 8-core host)
+    "tiny-cpu": dict(model="tiny", batch=8, seq=64, zero=0, cpu=True,
+                     desc="tiny TransformerLM (byte vocab 256, d_model 64, 2 blocks, 4 heads, MLP 256), CPU"),
 }
+
+TINY_STEPS = 50
+
+
+def run_tiny_cpu(args) -> int:
+    """CPU fallback: 50 AdamW steps (lr 1e-3, wd 0.01) on 8 x 64 uniform byte
+    ids from seed 0, then a checkpoint round trip (.uhfsbin) and greedy
+    generation of 32 bytes, through the public API.  Host wall-clock timing
+    (no device); the round trip and generation are checked, not timed."""
+    import torch
+
+    from underhfs_b200.nn import CrossEntropyLoss, TransformerLM
+    from underhfs_b200.optim import AdamW
+    from underhfs_b200.serialization import load_binary_state_tensors, save_binary_state_dict
+    from underhfs_b200.tensor import tensor
+
+    steps = args.steps if args.steps_given else TINY_STEPS
+    gen = torch.Generator().manual_seed(0)
+    batches = [torch.randint(0, 256, (8, 65), generator=gen) for _ in range(args.warmup + steps)]
+    model = TransformerLM(256, 64, 64, 256, 2, heads=4, seed=0)
+    opt = AdamW(model.parameters(), lr=1e-3, weight_decay=0.01)
+    loss_fn = CrossEntropyLoss()
+
+    def step(b):
+        opt.zero_grad()
+        loss = loss_fn(model(tensor(b[:, :64])).reshape(8 * 64, 256), tensor(b[:, 1:].reshape(-1)))
+        loss.backward()
+        opt.step()
+        return loss.item()
+
+    for i in range(args.warmup):
+        step(batches[i])
+    t0 = time.perf_counter()
+    losses = [step(batches[args.warmup + i]) for i in range(steps)]
+    dt = time.perf_counter() - t0
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "tiny.uhfsbin")
+        save_binary_state_dict(path, model.state_dict(as_tensors=True))
+        again = TransformerLM(256, 64, 64, 256, 2, heads=4, seed=1)
+        again.load_state_dict(load_binary_state_tensors(path))
+        probe = tensor(batches[0][:1, :64])
+        same = bool(torch.allclose(model(probe)._data.float(), again(probe)._data.float(), atol=1e-5))
+    out = model.generate(tensor(batches[0][0, :16]), 32)
+    tokens = 8 * 64 * steps
+    print(json.dumps({
+        "metric": "TransformerLM train tokens/sec (host wall clock, CPU fallback)", "value": tokens / dt,
+        "unit": "tokens/s", "n_gpus": 0, "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / steps,
+        "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "fp64 (CPU tensors)",
+        "data": "uniform byte ids in [0,256) from seed 0; random-init weights",
+        "config": {"model": CONFIGS["tiny-cpu"]["desc"], "global_batch": 8, "seq_len": 64, "parallelism": "none",
+                   "optimizer": "AdamW lr 1e-3 wd 0.01"},
+        "first_loss": losses[0], "final_loss": losses[-1], "checkpoint_roundtrip_matches": same,
+        "generated_tokens": int(out.shape[0]) - 16,
+    }))
+    return 0 if same else 1
+
+
+def run_reference_tiny(args) -> int:
+    """The same CPU configuration on the unmodified reference (baseline/_ref),
+    through its public API in a subprocess rooted there (this repository's own
+    ``underhfs`` package would otherwise shadow it).  Its TransformerLM has no
+    batch dimension or heads, so the 8 sequences of a step are accumulated
+    one by one before the optimizer step, single-head attention."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "underhfs" / "__init__.py").exists():
+        print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}))
+        return 0
+    steps = args.steps if args.steps_given else 1
+    code = f"""
+import json, random, time
+import underhfs
+from underhfs.nn import TransformerLM
+from underhfs.optim import AdamW
+from underhfs.functional import cross_entropy
+rng = random.Random(0)
+model = TransformerLM(256, 64, 64, 256, 2)
+opt = AdamW(model.parameters(), lr=1e-3, weight_decay=0.01)
+t0 = time.perf_counter()
+for _ in range({steps}):
+    opt.zero_grad()
+    for _ in range(8):
+        ids = [rng.randrange(256) for _ in range(65)]
+        loss = cross_entropy(model(underhfs.tensor(ids[:64])), underhfs.tensor(ids[1:]))
+        loss.backward()
+    opt.step()
+dt = time.perf_counter() - t0
+print(json.dumps({{"seconds": dt, "loss": loss.item()}}))
+"""
+    env = dict(os.environ, PYTHONPATH=str(ref))
+    proc = subprocess.run([sys.executable, "-c", code], cwd=str(ref), env=env, capture_output=True, text=True)
+    if proc.returncode != 0:
+        print(json.dumps({"impl": "reference", "unavailable": "reference run failed: "
+                          + (proc.stderr.strip().splitlines() or ["?"])[-1]}))
+        return 0
+    r = json.loads(proc.stdout.strip().splitlines()[-1])
+    print(json.dumps({
+        "impl": "reference", "metric": "TransformerLM train tokens/sec (host wall clock, CPU fallback)",
+        "value": 8 * 64 * steps / r["seconds"], "unit": "tokens/s", "n_gpus": 0, "steps": steps, "warmup": 0,
+        "ms_per_step": 1e3 * r["seconds"] / steps, "higher_is_better": True, "dtype": "Python float",
+        "data": "uniform byte ids in [0,256) from a seed", "final_loss": r["loss"],
+        "config": {"model": "reference TransformerLM(256, 64, 64, 256, 2), single head, 8 sequences accumulated "
+                   "per step", "global_batch": 8, "seq_len": 64},
+    }))
+    return 0
 
 
 def _clock_sampler(local_rank: int):
@@ -327,6 +439,11 @@ def main() -> int:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="125m-ddp",
                     help="125m-ddp is the headline run; the sharded configurations are measured the same way")
     args = ap.parse_args()
+    args.steps_given = "--steps" in sys.argv
+    if args.config == "tiny-cpu":
+        if "--warmup" not in sys.argv:
+            args.warmup = 3
+        return run_reference_tiny(args) if args.impl == "reference" else run_tiny_cpu(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
