@@ -231,3 +231,25 @@ def op_sweep(*, sizes=(1024, 4096, 8192), ew_elems: int = 1 << 26, iterations: i
             out["elementwise"].append({"op": name, "dtype": str(dt).replace("torch.", ""), "elements": ew_elems,
                                        "ms": ms, "gbs": nbytes / ms / 1e6})
     return out
+
+
+def main(argv: list[str] | None = None) -> int:
+    """``python -m underhfs_b200.benchmarks ops``: the op sweep as one JSON document
+    (bf16 GEMM at M=N=K 1024 / 4096 / 8192 against cuBLAS, add / mul on 2^26
+    elements in fp32 / fp16 / bf16)."""
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser(description="device-timed op microbenchmarks")
+    ap.add_argument("suite", choices=("ops",))
+    ap.add_argument("--iterations", type=int, default=20)
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        print(json.dumps({"suite": args.suite, "unavailable": "no CUDA device"}))
+        return 0
+    print(json.dumps(op_sweep(iterations=args.iterations), indent=2))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
