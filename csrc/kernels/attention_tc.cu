@@ -97,7 +97,10 @@ struct FwdArgs {
       a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
 
-template <int D>
+// kPolyExp: odd-indexed scores of each row use exp2_poly3 (FMA pipe) instead
+// of ex2.approx (MUFU), halving the MUFU work of the softmax (opt-in:
+// UHFS_ATTN_EXP=poly).
+template <int D, bool kPolyExp>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FwdArgs a) {
   using Cfg = FwdCfg<D>;
@@ -320,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < BKV / 2; ++i) {
         const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), a.sl2, -base));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), a.sl2, -base));
+        const float x1 = fmaf(__uint_as_float(sr[2 * i + 1]), a.sl2, -base);
+        const float p1 = kPolyExp ? exp2_poly3(x1) : ex2_approx(x1);
         rs4[(2 * i) & 3] += p0;
         rs4[(2 * i + 1) & 3] += p1;
         pk[i] = pack_bf16x2(p0, p1);
@@ -399,16 +403,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D>
+template <int D, bool kPolyExp>
 void launch_fwd(const AttnParams& p, cudaStream_t s) {
   using Cfg = FwdCfg<D>;
   static bool attr = false;
   if (!attr) {
-    UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D, kPolyExp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmem));
     // setmaxnreg redistributes exactly the launch allocation; any other
     // launch count would make the increase wait for registers that never come
     cudaFuncAttributes fa{};
-    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D>));
+    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, kPolyExp>));
     if (fa.numRegs != kLaunchRegs)
       throw std::runtime_error("fa_fwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
                                " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
@@ -429,7 +434,7 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
   a.status = device_status_ptr();
   a.trace = g_fwd_trace;
   dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
-  fa_fwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
+  fa_fwd_tc_kernel<D, kPolyExp><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -448,8 +453,17 @@ bool flash_attn_fwd_tc_supported(const AttnParams& p) {
 void set_attn_fwd_trace(unsigned long long* buf) { g_fwd_trace = buf; }
 
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s) {
-  if (p.D == 64) launch_fwd<64>(p, s);
-  else launch_fwd<128>(p, s);
+  static const bool poly = [] {
+    const char* e = getenv("UHFS_ATTN_EXP");
+    return e != nullptr && std::string(e) == "poly";
+  }();
+  if (p.D == 64) {
+    if (poly) launch_fwd<64, true>(p, s);
+    else launch_fwd<64, false>(p, s);
+  } else {
+    if (poly) launch_fwd<128, true>(p, s);
+    else launch_fwd<128, false>(p, s);
+  }
 }
 
 }  // namespace uhfs

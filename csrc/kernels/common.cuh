@@ -362,6 +362,28 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 2^x without the MUFU pipe (FMA and integer pipes only), for kernels whose
+// exponentials saturate MUFU: Cody-Waite range reduction x = k + f with
+// k = round(x) (the 1.5 * 2^23 addition trick) and |f| <= 1/2, a degree-3
+// polynomial for 2^f whose coefficients were fitted here by relative least
+// squares on [-1/2, 1/2] (max relative error 7.7e-5, ample for bf16
+// probabilities), and k added to the exponent field.  x < -125 returns 0
+// (masked scores are -inf).  tests/test_exp2_poly.py checks the same float32
+// steps against exp2.
+__device__ __forceinline__ float exp2_poly3(float x) {
+  const float xc = fmaxf(x, -125.f);
+  const float magic = 12582912.f;  // 1.5 * 2^23
+  const float t = __fadd_rn(xc, magic);
+  const int k = __float_as_int(t) - 0x4B400000;
+  const float f = __fsub_rn(xc, __fsub_rn(t, magic));
+  float p = fmaf(f, 0.05508868396282196f, 0.24260404706001282f);
+  p = fmaf(p, f, 0.6932762265205383f);
+  p = fmaf(p, f, 0.9999289512634277f);
+  // k is added to the exponent field in unsigned (modular) arithmetic
+  const float r = __uint_as_float(__float_as_uint(p) + ((unsigned)k << 23));
+  return x < -125.f ? 0.f : r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
