@@ -42,6 +42,11 @@ class SymmetricHeap {
 
 void comm_allreduce_f32(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
                         cudaStream_t s);
+// In-place fp32 all-reduce through an NVLink multicast object: `mc_base` is
+// the multicast address of the data buffer (every rank's copy bound to it);
+// `h` provides the signal pads of the barriers.
+void comm_allreduce_f32_nvls(const SymmetricHeap& h, uintptr_t mc_base, long long off_bytes, long long n, float scale,
+                             int blocks, cudaStream_t s);
 void comm_rs_adamw_ag(const SymmetricHeap& grads, long long g_off_bytes, const SymmetricHeap& params,
                       long long p_off_bytes, long long shard_lo, long long shard_n, uintptr_t master, uintptr_t m,
                       uintptr_t v, float lr, float beta1, float beta2, float eps, float weight_decay,

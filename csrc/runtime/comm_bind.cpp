@@ -100,6 +100,10 @@ void bind_comm(py::module_& m) {
       });
   m.def("comm_allreduce_f32", [](const SymmetricHeap& h, long long off, long long n, float scale, int blocks,
                                  uintptr_t s) { comm_allreduce_f32(h, off, n, scale, blocks, S(s)); });
+  m.def("comm_allreduce_f32_nvls", [](const SymmetricHeap& h, uintptr_t mc, long long off, long long n, float scale,
+                                      int blocks, uintptr_t s) {
+    comm_allreduce_f32_nvls(h, mc, off, n, scale, blocks, S(s));
+  });
   m.def("comm_rs_adamw_ag",
         [](const SymmetricHeap& g, long long goff, const SymmetricHeap& p, long long poff, long long lo, long long n,
            uintptr_t master, uintptr_t mm, uintptr_t vv, float lr, float b1, float b2, float eps, float wd,

@@ -120,6 +120,54 @@ def case_ddp(rank: int, world: int) -> None:
     assert core().device_status(True)["code"] == 0
 
 
+def case_nvls(rank: int, world: int) -> None:
+    """DDP gradients reduced in the NVSwitch (multimem) match NCCL's.
+
+    A rank whose memory is bound to an NVLink multicast object must not die
+    while a peer still uses it: every rank finishes its GPU work, the ranks
+    agree on the outcome with a collective, release the buffers and meet at a
+    barrier before either reports a failure."""
+    import gc
+
+    os.environ["UNDERHFS_NVLS"] = "1"
+    from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
+    from underhfs_b200.ops._lib import core
+
+    gen = torch.Generator().manual_seed(400 + rank)
+    ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+    tg = torch.roll(ids, -1, 1)
+    ref_model = _model()
+    ref_model.zero_grad()
+    ref_model(ids, tg).backward()
+    ref = ref_model.flat.grads.clone()
+    dist.all_reduce(ref)
+    ref /= world
+    model = _model()
+    ddp = DistributedDataParallel(model, policy_from_env(), bucket_mb=0.25)
+    problems = []
+    if ddp._bucketer.mc == 0:
+        problems.append("no multicast address: NVLS not in use")
+    else:
+        for _ in range(2):
+            model.zero_grad()
+            ddp(ids, tg).backward()
+            ddp.synchronize_gradients()
+            torch.cuda.synchronize()
+            err = ((model.flat.grads[: ref.numel()] - ref).abs().max() / ref.abs().max()).item()
+            if not err < 1e-4:
+                problems.append(f"gradient error {err}")
+    torch.cuda.synchronize()
+    if core().device_status(True)["code"] != 0:
+        problems.append("device status")
+    ok = torch.tensor([0 if problems else 1], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank learns the outcome
+    del ddp, model
+    gc.collect()
+    torch.cuda.synchronize()
+    dist.barrier()
+    assert ok.item() == 1, (rank, problems)
+
+
 def case_zero(rank: int, world: int) -> None:
     from underhfs_b200.optim import FusedAdamW, ZeroAwareAdamW, ZeroShard
 
@@ -272,7 +320,7 @@ def main() -> int:
     rank, world = _setup()
     try:
         cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3,
-                 "native": case_native, "cp": case_cp}
+                 "native": case_native, "cp": case_cp, "nvls": case_nvls}
         cases[case](rank, world)
         dist.barrier()
         if rank == 0:

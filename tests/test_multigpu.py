@@ -32,10 +32,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero", "zero3", "native", "cp"])
+@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero", "zero3", "native", "cp", "nvls"])
 def test_two_gpu_case(case):
     if _gpus() < 2:
         pytest.skip("needs two GPUs")
+    if case == "nvls" and os.environ.get("UNDERHFS_TEST_NVLS") != "1":
+        pytest.skip("NVLS (multimem) all-reduce is opt-in: UNDERHFS_TEST_NVLS=1 runs its check")
     env = dict(os.environ)
     env["PYTHONPATH"] = str(ROOT) + os.pathsep + env.get("PYTHONPATH", "")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",

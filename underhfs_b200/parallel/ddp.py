@@ -17,6 +17,8 @@ parameter after backward, no overlap).
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from underhfs_b200.ops._lib import core
@@ -36,8 +38,16 @@ class BucketedAllReduce:
         self.use_nccl = use_nccl
         flat = model.flat
         n = (flat.numel + 3) // 4 * 4
-        self.sym = SymmetricBuffer(n * 4, rank=self.rank, world=self.world)
-        grads = self.sym.tensor(n, torch.float32)
+        # UNDERHFS_NVLS=1: gradients in memory bound to an NVLink multicast
+        # object (allocated through torch's symmetric memory), reduced in the
+        # switch by allreduce_nvls_f32_kernel; this heap then only carries the
+        # barrier signal pads.  Falls back to the peer-to-peer kernel when the
+        # system offers no multicast.
+        self.mc = 0
+        grads = self._nvls_grads(n) if os.environ.get("UNDERHFS_NVLS", "0") == "1" and not use_nccl else None
+        self.sym = SymmetricBuffer(4096 if grads is not None else n * 4, rank=self.rank, world=self.world)
+        if grads is None:
+            grads = self.sym.tensor(n, torch.float32)
         model.rehome_buffers(grads=grads)
         self.flat = model.flat
         self.n = n
@@ -53,10 +63,31 @@ class BucketedAllReduce:
         # UNDERHFS_DDP_TRACE=1: CUDA events around every bucket (eager steps
         # only) and a per-step report of how much reduction time overlapped
         # the backward kernels
-        import os
-
         self.trace = os.environ.get("UNDERHFS_DDP_TRACE", "0") == "1"
         self._trace_events: list = []
+
+    def _nvls_grads(self, n: int):
+        """fp32 [n] gradient buffer bound to a multicast object, or None."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        try:
+            group = dist.group.WORLD
+            if hasattr(symm_mem, "enable_symm_mem_for_group"):
+                symm_mem.enable_symm_mem_for_group(group.group_name)
+            buf = symm_mem.empty(n, dtype=torch.float32, device=torch.device("cuda", torch.cuda.current_device()))
+            handle = symm_mem.rendezvous(buf, group.group_name)
+            mc = int(handle.multicast_ptr)
+        except Exception as e:  # no symmetric memory / multicast on this system
+            print(f"[ddp] NVLS unavailable ({type(e).__name__}: {e}); using the peer-to-peer all-reduce", flush=True)
+            return None
+        if mc == 0:
+            print("[ddp] NVLS unavailable (no multicast support); using the peer-to-peer all-reduce", flush=True)
+            return None
+        self._nvls_handle = handle  # keeps the mapping alive
+        self.mc = mc + (buf.data_ptr() - int(handle.buffer_ptrs[handle.rank]))
+        buf.zero_()
+        return buf
 
     def arm(self, enabled: bool = True) -> None:
         self._next = 0
@@ -89,6 +120,9 @@ class BucketedAllReduce:
                 dist.all_reduce(view)
                 if self.scale != 1.0:
                     view.mul_(self.scale)
+            elif self.mc:
+                core().comm_allreduce_f32_nvls(self.sym.heap, self.mc, lo * 4, hi - lo, self.scale, self.blocks,
+                                               self.stream.cuda_stream)
             else:
                 core().comm_allreduce_f32(self.sym.heap, lo * 4, hi - lo, self.scale, self.blocks,
                                           self.stream.cuda_stream)
