@@ -106,3 +106,31 @@ def test_transformer_lm_batched_multihead_shapes():
     loss = lm(tensor([[1, 2, 3], [4, 5, 6]]), tensor([[2, 3, 4], [5, 6, 7]]))
     loss.backward()
     assert all(p.grad is not None for p in lm.parameters())
+
+
+def test_step_split_without_flat_buffer_is_one_step():
+    """AdamW.step_split on ordinary (non-flat) parameters waits, then takes one
+    normal step: same parameters and step count as step()."""
+    import torch
+
+    from underhfs_b200.nn import Linear
+    from underhfs_b200.optim import AdamW
+    from underhfs_b200.tensor import tensor
+
+    torch.manual_seed(0)
+    a, b = Linear(4, 3), Linear(4, 3)
+    for pa, pb in zip(a.parameters(), b.parameters()):
+        pb._data.data.copy_(pa._data)
+    oa = AdamW(a.parameters(), lr=1e-2, weight_decay=0.1)
+    ob = AdamW(b.parameters(), lr=1e-2, weight_decay=0.1)
+    x = tensor([[1.0, -2.0, 0.5, 3.0]])
+    waited = []
+    for _ in range(3):
+        for m, o in ((a, oa), (b, ob)):
+            o.zero_grad()
+            m(x).sum().backward()
+        oa.step()
+        ob.step_split(2, lambda: waited.append(1))
+    assert len(waited) == 3 and oa.step_count == ob.step_count == 3
+    for (na, pa), (nb, pb) in zip(a.named_parameters(), b.named_parameters()):
+        assert na == nb and torch.equal(pa._data, pb._data)

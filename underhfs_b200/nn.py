@@ -120,12 +120,15 @@ class Module:
             p.zero_grad()
 
     def state_dict(self, *, as_tensors: bool = False) -> dict[str, Any]:
-        """Nested Python lists like the reference, or detached fp32 CPU torch
-        tensors with ``as_tensors=True`` (what large checkpoints use)."""
+        """Nested Python lists like the reference (exact: the parameter's own
+        values, widened to Python floats), or detached fp32 CPU torch tensors
+        with ``as_tensors=True`` (what large checkpoints use).  The live
+        parameter is read, not an fp32 master copy: under ZeRO a rank's master
+        is current only for its own shard."""
         out: dict[str, Any] = {}
         for name, p in self.named_parameters():
-            value = p._data.detach().float().cpu()
-            out[name] = value.clone() if as_tensors else value.double().tolist()
+            value = p._data.detach()
+            out[name] = value.float().cpu().clone() if as_tensors else value.double().cpu().tolist()
         return out
 
     def load_state_dict(self, state: dict[str, Any]) -> None:
