@@ -59,3 +59,21 @@ def test_zero3_engine_has_every_engine_hook():
     for name in ("context_attention", "positions"):
         assert hasattr(eng, name) and getattr(eng, name) is None
     assert issubclass(Zero3Engine, LMEngine)
+
+
+@pytest.mark.parametrize("tied", [True, False])
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_unit_shard_ranges_are_contiguous_for_moment_staging(tied, world):
+    """Moment offload copies each unit's [shard_lo, shard_lo + shard_len) as
+    one block: the unit ranges must tile the shard in order and contain every
+    segment of the unit."""
+    spec = LMSpec(1024, 256, 256, 1024, 3, heads=4, tied=tied)
+    z = _units(spec, 0, world)
+    cursor = 0
+    for key in ["embed"] + list(range(spec.layers)) + ["tail"]:
+        u = z.units[key]
+        assert u.shard_lo == cursor
+        for _nat, soff, ln in u.segs:
+            assert u.shard_lo <= soff and soff + ln <= u.shard_lo + u.shard_len
+        cursor += u.shard_len
+    assert cursor <= z.shard_total
