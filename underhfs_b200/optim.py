@@ -217,6 +217,7 @@ class AdamW(Optimizer):
         if self._flat is not None:
             self._flat_step(b1, b2)
             return
+        cpu: list = []
         for i, p in enumerate(self.params):
             g = p.grad
             if g is None:
@@ -224,7 +225,9 @@ class AdamW(Optimizer):
             if p.device.kind == "cuda":
                 self._cuda_step(i, p, g, b1, b2)
             else:
-                self._cpu_step(i, p, g, b1, b2)
+                cpu.append((i, p, g))
+        if cpu:
+            self._cpu_steps(cpu, b1, b2)
 
     def _flat_step(self, b1: float, b2: float, lo: int = 0, hi: int | None = None, increment: bool = True) -> None:
         from underhfs_b200.ops import kernels as K
@@ -275,20 +278,27 @@ class AdamW(Optimizer):
             pd.copy_(master if in_place else master.to(pd.dtype))
         p.backend = "native_cuda"
 
-    def _cpu_step(self, i: int, p: Tensor, g: Tensor, b1: float, b2: float) -> None:
+    def _cpu_steps(self, items: list, b1: float, b2: float) -> None:
+        """Every CPU parameter in one pass of multi-tensor (foreach) ops; the
+        per-element arithmetic and its order are those of the single-tensor
+        update (weight decay multiplied, then added)."""
         with torch.no_grad():
-            pd = p._data
-            gd = g._data.to(pd.dtype)
+            pds = [p._data for _, p, _ in items]
+            gds = [g._data.to(p._data.dtype) for _, p, g in items]
             if self.decoupled:
-                pd.mul_(1.0 - self.lr * self.weight_decay)
+                torch._foreach_mul_(pds, 1.0 - self.lr * self.weight_decay)
             else:
-                gd = gd + self.weight_decay * pd
-            m, v = self._m32[i], self._v32[i]
-            m.mul_(b1).add_(gd, alpha=1 - b1)
-            v.mul_(b2).addcmul_(gd, gd, value=1 - b2)
-            mh = m / (1 - b1 ** self.step_count)
-            vh = v / (1 - b2 ** self.step_count)
-            pd.add_(mh / (vh.sqrt() + self.eps), alpha=-self.lr)
+                gds = torch._foreach_add(gds, torch._foreach_mul(pds, self.weight_decay))
+            ms = [self._m32[i] for i, _, _ in items]
+            vs = [self._v32[i] for i, _, _ in items]
+            torch._foreach_mul_(ms, b1)
+            torch._foreach_add_(ms, gds, alpha=1 - b1)
+            torch._foreach_mul_(vs, b2)
+            torch._foreach_addcmul_(vs, gds, gds, value=1 - b2)
+            mh = torch._foreach_div(ms, 1 - b1 ** self.step_count)
+            den = torch._foreach_sqrt(torch._foreach_div(vs, 1 - b2 ** self.step_count))
+            torch._foreach_add_(den, self.eps)
+            torch._foreach_add_(pds, torch._foreach_div(mh, den), alpha=-self.lr)
 
 
 class FusedAdamW(AdamW):
