@@ -51,8 +51,16 @@ PYBIND11_MODULE(_core, m) {
   m.doc() = "underhfs_b200 native core: sm_100a kernels and C++ runtime";
   m.attr("__version__") = "0.2.0";
   m.attr("cuda_enabled") = true;
-  m.attr("cudnn_enabled") = true;  // conv2d kernels present (own implementation, no cuDNN)
+#ifdef UHFS_NO_CONV
+  m.attr("cudnn_enabled") = false;  // built with UNDERHFS_WITH_CUDNN=OFF: no conv2d kernels
+#else
+  m.attr("cudnn_enabled") = true;  // conv2d kernels present (own implicit-GEMM kernels, no cuDNN)
+#endif
+#ifdef UHFS_NO_NCCL
+  m.attr("nccl_enabled") = false;  // built with UNDERHFS_WITH_NCCL=OFF
+#else
   m.attr("nccl_enabled") = true;
+#endif
   m.attr("arch") = "sm_100a";
 
   // --------------------------------------------------------- CPU contract
@@ -84,9 +92,11 @@ PYBIND11_MODULE(_core, m) {
         py::arg("v"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"),
         py::arg("step"));
   m.def("cuda_attention_f32", &cuda_attention_f32_host);
+#ifndef UHFS_NO_CONV
   m.def("cudnn_conv2d_forward_f32", &conv2d_forward_f32_host);
   m.def("cudnn_conv2d_backward_input_f32", &conv2d_backward_input_f32_host);
   m.def("cudnn_conv2d_backward_weight_f32", &conv2d_backward_weight_f32_host);
+#endif
 
   m.def("cuda_allocator_stats", []() {
     AllocatorStats s = allocator_stats();

@@ -500,11 +500,10 @@ __global__ void __launch_bounds__(128) fa_bwd_kernel(const AttnBwdParams p) {
 template <int D>
 void fwd_impl(const AttnParams& p, cudaStream_t s) {
   constexpr int smem = 128 * D * 2 + 4 * 64 * D * 2;
-  static bool set = false;
-  if (!set) {
+  static PerDeviceOnce once;
+  once([] {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    set = true;
-  }
+  });
   dim3 grid((p.T + 127) / 128, p.B * p.H);
   fa_fwd_kernel<D><<<grid, 256, smem, s>>>(p);
   note_launch();
@@ -513,11 +512,10 @@ void fwd_impl(const AttnParams& p, cudaStream_t s) {
 template <int D>
 void bwd_impl(const AttnBwdParams& p, cudaStream_t s) {
   constexpr int smem = 6 * 64 * D * 2 + 64 * 64 * 2 + 4 * 64 * 4;
-  static bool set = false;
-  if (!set) {
+  static PerDeviceOnce once;
+  once([] {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    set = true;
-  }
+  });
   const long long rows = (long long)p.f.B * p.f.T * p.f.H;
   const long long rows_per_block = 256 / (D / 8);
   int g1 = (int)((rows + rows_per_block - 1) / rows_per_block);

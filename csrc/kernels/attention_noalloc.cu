@@ -22,9 +22,15 @@
 // message, never truncated.  Example: B=2, T=1024, H=8, D=128 uses 8.06 MiB.
 //
 // Use rules:
-//   * The first call on a device looks up the device address of the array
-//     (cudaGetSymbolAddress) with that device current.  Make that first call
-//     before any CUDA stream capture begins.
+//   * The first call on a device looks up, with that device current, the
+//     device addresses of the scratch array and of the library's device status
+//     word (both static __device__ objects, resolved with cudaGetSymbolAddress;
+//     neither lookup allocates), and sets the kernel's shared-memory attribute.
+//     Make that first call before any CUDA stream capture begins.
+//   * The kernels' waits are bounded: a wait that runs out records a code in
+//     the device status word and the kernel returns early, so the call itself
+//     still returns 0.  Read (and optionally clear) that word with
+//     uhfs_flash_attn_bwd_noalloc_status() after the stream has finished.
 //   * All calls on a device share the one array and nothing is cleared between
 //     calls except what the kernels initialise themselves (the dQ accumulator
 //     is zeroed by the first kernel of every call; delta is fully rewritten).
@@ -42,6 +48,7 @@
 
 #include "attention_noalloc.h"
 #include "kernels.h"
+#include "../runtime/runtime.h"
 
 namespace uhfs {
 namespace {
@@ -53,7 +60,9 @@ static __device__ __align__(256) unsigned char g_attn_bwd_scratch[kScratchBytes]
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
-char g_last_error[256] = "";
+// One message per host thread, so calls from different threads (on the same or
+// different devices) do not overwrite each other's message.
+thread_local char g_last_error[256] = "";
 
 void set_error(const char* msg) {
   std::snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
@@ -86,7 +95,7 @@ __attribute__((visibility("default"))) unsigned long long uhfs_flash_attn_bwd_no
   return (unsigned long long)uhfs::kScratchBytes;
 }
 
-// Message of the last failed call ("" after success).
+// Message of the last failed call made by the calling host thread ("" after success).
 __attribute__((visibility("default"))) const char* uhfs_flash_attn_bwd_noalloc_error() { return uhfs::g_last_error; }
 
 // Backward of causal / full multi-head attention over a fused QKV projection.
@@ -98,6 +107,22 @@ __attribute__((visibility("default"))) const char* uhfs_flash_attn_bwd_noalloc_e
 // head_dim D must be 64 or 128.  `stream` is a cudaStream_t (0 = legacy default).
 // Returns 0 on success, 1 for invalid arguments, 2 when the problem needs more
 // scratch than uhfs_flash_attn_bwd_noalloc_capacity(), 3 for a CUDA error.
+// Device status word of the current device: returns the first error code a
+// kernel of this library recorded there (0 = none; 1-3 a bounded wait on the
+// GPU ran out, 4 a peer wait ran out, 5 a bounds check failed), and clears the
+// word when `clear` is non-zero.  Reads with a synchronous cudaMemcpy, so call
+// it after the work has finished (and outside stream capture); returns -1 if
+// the word cannot be read.
+__attribute__((visibility("default"))) int uhfs_flash_attn_bwd_noalloc_status(int clear) {
+  try {
+    const uhfs::DeviceStatusHost st = uhfs::read_device_status(clear != 0);
+    return st.code;
+  } catch (const std::exception& e) {
+    uhfs::set_error(e.what());
+    return -1;
+  }
+}
+
 __attribute__((visibility("default"))) int uhfs_flash_attn_bwd_noalloc(const void* qkv, const void* o,
                                                                       const float* lse, const void* dout,
                                                                       void* dqkv, int B, int T, int H, int D,

@@ -91,11 +91,19 @@ struct FwdArgs {
   unsigned long long* trace;
 };
 
+// Compiled in only with -DUHFS_ATTN_TRACE (UNDERHFS_ATTN_TRACE=1 at build
+// time); the product build has no stamps and no trace pointer test.
+#ifdef UHFS_ATTN_TRACE
 #define FWD_TRACE(ev, step)                                                                              \
   do {                                                                                                   \
     if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
       a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
+#else
+#define FWD_TRACE(ev, step) \
+  do { \
+  } while (0)
+#endif
 
 // kPolyExp: odd-indexed scores of each row use exp2_poly3 (FMA pipe) instead
 // of ex2.approx (MUFU), halving the MUFU work of the softmax (opt-in:
@@ -406,8 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D, bool kPolyExp>
 void launch_fwd(const AttnParams& p, cudaStream_t s) {
   using Cfg = FwdCfg<D>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce once;
+  once([] {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D, kPolyExp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmem));
     // setmaxnreg redistributes exactly the launch allocation; any other
@@ -417,8 +425,7 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
     if (fa.numRegs != kLaunchRegs)
       throw std::runtime_error("fa_fwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
                                " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
-    attr = true;
-  }
+  });
   const long long F = (long long)p.H * D;
   // q, k, v are column blocks of one [B*T, 3F] matrix (the fused projection)
   CUtensorMap tm = make_tmap_bf16_2d(p.q, (uint64_t)(3 * F), (uint64_t)p.B * p.T, (uint64_t)p.q_stride_t, 64, 128);
@@ -450,7 +457,15 @@ bool flash_attn_fwd_tc_supported(const AttnParams& p) {
          (reinterpret_cast<uintptr_t>(p.o) & 15u) == 0 && (p.o_stride_t % 8) == 0;
 }
 
-void set_attn_fwd_trace(unsigned long long* buf) { g_fwd_trace = buf; }
+void set_attn_fwd_trace(unsigned long long* buf) {
+#ifdef UHFS_ATTN_TRACE
+  g_fwd_trace = buf;
+#else
+  if (buf != nullptr)
+    throw std::runtime_error("set_attn_fwd_trace: the extension was built without UHFS_ATTN_TRACE "
+                             "(rebuild with UNDERHFS_ATTN_TRACE=1)");
+#endif
+}
 
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s) {
   static const bool poly = [] {

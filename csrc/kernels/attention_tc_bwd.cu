@@ -116,11 +116,19 @@ struct BwdArgs {
   unsigned long long* trace;
 };
 
+// Compiled in only with -DUHFS_ATTN_TRACE (UNDERHFS_ATTN_TRACE=1 at build
+// time); the product build has no stamps and no trace pointer test.
+#ifdef UHFS_ATTN_TRACE
 #define BWD_TRACE(ev, step)                                                                              \
   do {                                                                                                   \
     if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
       a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
+#else
+#define BWD_TRACE(ev, step) \
+  do { \
+  } while (0)
+#endif
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -549,8 +557,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D>
 void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   using Cfg = BwdCfg<D>;
-  static bool attr = false;
-  if (!attr) {
+  static PerDeviceOnce once;
+  once([] {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem));
     // setmaxnreg redistributes the launch allocation; a different launch count
     // could make the increase wait for registers that never come
@@ -559,8 +567,7 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
     if (fa.numRegs != kLaunchRegs)
       throw std::runtime_error("fa_bwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
                                " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
-    attr = true;
-  }
+  });
   const long long F = (long long)p.f.H * D;
   CUtensorMap tq = make_tmap_bf16_2d(p.f.q, (uint64_t)(3 * F), (uint64_t)p.f.B * p.f.T, (uint64_t)(3 * F), 64, 128);
   CUtensorMap td = make_tmap_bf16_2d(p.dout, (uint64_t)F, (uint64_t)p.f.B * p.f.T, (uint64_t)p.do_stride_t, 64, 128);
@@ -600,7 +607,15 @@ bool flash_attn_bwd_tc_supported(const AttnBwdParams& p) {
          (reinterpret_cast<uintptr_t>(p.f.q) & 15u) == 0;
 }
 
-void set_attn_bwd_trace(unsigned long long* buf) { g_bwd_trace = buf; }
+void set_attn_bwd_trace(unsigned long long* buf) {
+#ifdef UHFS_ATTN_TRACE
+  g_bwd_trace = buf;
+#else
+  if (buf != nullptr)
+    throw std::runtime_error("set_attn_bwd_trace: the extension was built without UHFS_ATTN_TRACE "
+                             "(rebuild with UNDERHFS_ATTN_TRACE=1)");
+#endif
+}
 
 void flash_attn_bwd_tc_main(const AttnBwdParams& p, cudaStream_t s) {
   if (p.f.D == 64) launch_bwd<64>(p, s);

@@ -614,8 +614,27 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Launch accounting shared with the host runtime (stream stats contract).
 void note_launch();
-// Per-device status word for bounded waits (zeroed at first use).
+// Per-device status word for bounded waits: a static __device__ object of
+// the runtime module, resolved per device with cudaGetSymbolAddress (never
+// allocates).
 DeviceStatus* device_status_ptr();
+
+// Runs a set-up step (cudaFuncSetAttribute and the like) once per device.
+// Function attributes are per device, so a flag shared by every device would
+// skip the set-up on the second GPU a process launches on.  Concurrent first
+// calls may both run the step, which must therefore be idempotent.
+struct PerDeviceOnce {
+  unsigned long long mask = 0;  // bit d: done on device d (ordinals 0..63)
+  template <class F>
+  void operator()(F&& f) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (__atomic_load_n(&mask, __ATOMIC_ACQUIRE) & bit) return;
+    f();
+    __atomic_fetch_or(&mask, bit, __ATOMIC_ACQ_REL);
+  }
+};
 
 }  // namespace uhfs
 

@@ -891,12 +891,14 @@ CUtensorMap make_tmap(const void* base, uint64_t inner, uint64_t outer, uint64_t
 }
 
 int num_sms() {
-  static int n = 0;
+  static int by_dev[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& n = by_dev[dev & 63];
   if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n = v > 0 ? v : 148;
   }
   return n;
 }
@@ -923,11 +925,8 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   constexpr int kSmem = Cfg::kSmemBytes + kEpiWarps * epi_boxes(EPI) * kEpiBox;
   static_assert(kSmem <= 227 * 1024, "gemm shared memory");
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    attr_set = true;
-  }
+  static PerDeviceOnce once;
+  once([&] { UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem)); });
   // A: K-major [M][lda] -> dims {K, M}; MN-major [K][lda] -> dims {M, K}
   CUtensorMap ta = A_MN ? make_tmap(p.A, p.M, p.K, p.lda, BK) : make_tmap(p.A, p.K, p.M, p.lda, BM);
   CUtensorMap tb = B_MN ? make_tmap(p.B, p.N, p.K, p.ldb, BK) : make_tmap(p.B, p.K, p.N, p.ldb, BN);
@@ -1021,11 +1020,15 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   constexpr int kSmem = pair_smem_bytes(EPI);
   static_assert(kSmem <= 227 * 1024, "pair gemm shared memory");
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
-  static int clusters = 0;
-  if (clusters == 0) {
+  static int clusters_by_dev[64] = {0};
+  static PerDeviceOnce once;
+  int dev = 0;
+  UHFS_CUDA_CHECK(cudaGetDevice(&dev));
+  once([&] {
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    clusters = max_pair_clusters(kern, kSmem);
-  }
+    clusters_by_dev[dev & 63] = max_pair_clusters(kern, kSmem);
+  });
+  const int clusters = clusters_by_dev[dev & 63];
   // Each CTA stages 128 rows of A and 128 rows of B per k-block.
   CUtensorMap ta = A_MN ? make_tmap(p.A, p.M, p.K, p.lda, BK) : make_tmap(p.A, p.K, p.M, p.lda, kPairHalf);
   CUtensorMap tb = B_MN ? make_tmap(p.B, p.N, p.K, p.ldb, BK) : make_tmap(p.B, p.K, p.N, p.ldb, kPairHalf);

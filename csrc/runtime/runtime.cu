@@ -1,7 +1,9 @@
 // Host runtime: stream stats, caching allocator, device status word,
 // TensorCore, CudaTensor storage, one-shot host helpers and the NCCL process
 // group.  See runtime.h for the reference contracts each piece keeps.
+#ifndef UHFS_NO_NCCL
 #include <nccl.h>
+#endif
 
 #include <atomic>
 #include <cmath>
@@ -51,21 +53,27 @@ StreamStats stream_stats() {
 }
 
 namespace {
+// One status word per GPU, in this library's own static device memory: the
+// word exists as soon as the module is loaded on a device (zero-initialised)
+// and looking it up allocates nothing, so every entry point -- including the
+// allocation-free ones -- can hand it to a kernel.
+__device__ DeviceStatus g_device_status;
+constexpr int kMaxStatusDevices = 64;
 std::mutex g_status_mu;
-std::unordered_map<int, DeviceStatus*> g_status;
+DeviceStatus* g_status[kMaxStatusDevices] = {nullptr};
 }  // namespace
 
 DeviceStatus* device_status_ptr() {
   int dev = 0;
   UHFS_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxStatusDevices) throw std::runtime_error("device ordinal out of range for status word");
   std::lock_guard<std::mutex> lk(g_status_mu);
-  auto it = g_status.find(dev);
-  if (it != g_status.end()) return it->second;
-  DeviceStatus* p = nullptr;
-  UHFS_CUDA_CHECK(cudaMalloc(&p, sizeof(DeviceStatus)));
-  UHFS_CUDA_CHECK(cudaMemset(p, 0, sizeof(DeviceStatus)));
-  g_status[dev] = p;
-  return p;
+  if (g_status[dev] == nullptr) {
+    void* p = nullptr;
+    UHFS_CUDA_CHECK(cudaGetSymbolAddress(&p, g_device_status));
+    g_status[dev] = static_cast<DeviceStatus*>(p);
+  }
+  return g_status[dev];
 }
 
 DeviceStatusHost read_device_status(bool clear) {
@@ -426,6 +434,7 @@ std::vector<float> conv2d_backward_weight_f32_host(const std::vector<float>& dyv
   return d2h(ddw.p, (size_t)K * C * R * S);
 }
 
+#ifndef UHFS_NO_NCCL
 // ------------------------------------------------------------------- NCCL
 namespace {
 void nccl_check(ncclResult_t r, const char* what) {
@@ -549,5 +558,29 @@ void NcclProcessGroup::all_gather_ptr(uintptr_t send, uintptr_t recv, int64_t se
              "all_gather");
   (void)dt_bytes;
 }
+
+#else  // UHFS_NO_NCCL: built with UNDERHFS_WITH_NCCL=OFF
+namespace {
+[[noreturn]] void no_nccl() {
+  throw std::runtime_error("NCCL process groups need the native core built with UNDERHFS_WITH_NCCL=ON");
+}
+}  // namespace
+std::string nccl_create_unique_id_hex() { no_nccl(); }
+NcclProcessGroup::NcclProcessGroup(int rank, int world_size, const std::string&, int device)
+    : rank_(rank), world_(world_size), device_(device) {
+  no_nccl();
+}
+NcclProcessGroup::~NcclProcessGroup() {}
+std::vector<float> NcclProcessGroup::staged(const std::vector<float>&, size_t, int, int) { no_nccl(); }
+void NcclProcessGroup::barrier() { no_nccl(); }
+std::vector<float> NcclProcessGroup::all_reduce_sum(const std::vector<float>&) { no_nccl(); }
+std::vector<float> NcclProcessGroup::broadcast(const std::vector<float>&, int) { no_nccl(); }
+std::vector<float> NcclProcessGroup::reduce_scatter(const std::vector<float>&) { no_nccl(); }
+std::vector<float> NcclProcessGroup::all_gather(const std::vector<float>&) { no_nccl(); }
+void NcclProcessGroup::all_reduce_ptr(uintptr_t, int64_t, int, uintptr_t) { no_nccl(); }
+void NcclProcessGroup::broadcast_ptr(uintptr_t, int64_t, int, int, uintptr_t) { no_nccl(); }
+void NcclProcessGroup::reduce_scatter_ptr(uintptr_t, uintptr_t, int64_t, int, uintptr_t) { no_nccl(); }
+void NcclProcessGroup::all_gather_ptr(uintptr_t, uintptr_t, int64_t, int, uintptr_t) { no_nccl(); }
+#endif  // UHFS_NO_NCCL
 
 }  // namespace uhfs

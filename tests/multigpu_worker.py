@@ -133,32 +133,39 @@ def case_nvls(rank: int, world: int) -> None:
     from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
     from underhfs_b200.ops._lib import core
 
-    gen = torch.Generator().manual_seed(400 + rank)
-    ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
-    tg = torch.roll(ids, -1, 1)
-    ref_model = _model()
-    ref_model.zero_grad()
-    ref_model(ids, tg).backward()
-    ref = ref_model.flat.grads.clone()
-    dist.all_reduce(ref)
-    ref /= world
-    model = _model()
-    ddp = DistributedDataParallel(model, policy_from_env(), bucket_mb=0.25)
     problems = []
-    if ddp._bucketer.mc == 0:
-        problems.append("no multicast address: NVLS not in use")
-    else:
-        for _ in range(2):
-            model.zero_grad()
-            ddp(ids, tg).backward()
-            ddp.synchronize_gradients()
-            torch.cuda.synchronize()
-            err = ((model.flat.grads[: ref.numel()] - ref).abs().max() / ref.abs().max()).item()
-            if not err < 1e-4:
-                problems.append(f"gradient error {err}")
-    torch.cuda.synchronize()
-    if core().device_status(True)["code"] != 0:
-        problems.append("device status")
+    ddp = model = None
+    try:
+        gen = torch.Generator().manual_seed(400 + rank)
+        ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+        tg = torch.roll(ids, -1, 1)
+        ref_model = _model()
+        ref_model.zero_grad()
+        ref_model(ids, tg).backward()
+        ref = ref_model.flat.grads.clone()
+        dist.all_reduce(ref)
+        ref /= world
+        model = _model()
+        # from here on this rank's gradients may be bound to the multicast object
+        ddp = DistributedDataParallel(model, policy_from_env(), bucket_mb=0.25)
+        if ddp._bucketer.mc == 0:
+            problems.append("no multicast address: NVLS not in use")
+        else:
+            for _ in range(2):
+                model.zero_grad()
+                ddp(ids, tg).backward()
+                ddp.synchronize_gradients()
+                torch.cuda.synchronize()
+                err = ((model.flat.grads[: ref.numel()] - ref).abs().max() / ref.abs().max()).item()
+                if not err < 1e-4:
+                    problems.append(f"gradient error {err}")
+        torch.cuda.synchronize()
+        if core().device_status(True)["code"] != 0:
+            problems.append("device status")
+    except Exception as exc:  # recorded, never raised before the ranks agree
+        problems.append(f"{type(exc).__name__}: {exc}")
+    # every rank reaches the agreement, the release and the barrier, whatever
+    # happened above, so no rank exits while a peer still uses its memory
     ok = torch.tensor([0 if problems else 1], device="cuda")
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank learns the outcome
     del ddp, model

@@ -31,11 +31,44 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
+def _on(name: str, default: str = "ON") -> bool:
+    """Build option from the environment: ON/1/TRUE/YES (any case) is on."""
+    return os.environ.get(name, default).strip().upper() in ("ON", "1", "TRUE", "YES")
+
+
+def options() -> dict[str, bool]:
+    """The build options, named like the reference's CMake options
+    (CMakeLists.txt:4-6) but on by default, since this framework exists for
+    the GPU:
+
+    * ``UNDERHFS_WITH_CUDA`` -- build the native core at all (OFF: a pure
+      Python install whose CPU paths run on torch; ``native.probe()``
+      reports the core as unavailable);
+    * ``UNDERHFS_WITH_NCCL`` -- link NCCL for ``NcclProcessGroup`` (OFF: the
+      class raises, ``nccl_enabled`` is False; the NVLink comm kernels do not
+      need NCCL and stay);
+    * ``UNDERHFS_WITH_CUDNN`` -- expose the conv2d entry points (this
+      framework's own implicit-GEMM kernels, not cuDNN; the name is kept for
+      build-script compatibility).  OFF: ``cudnn_enabled`` is False.
+    """
+    return {"cuda": _on("UNDERHFS_WITH_CUDA"), "nccl": _on("UNDERHFS_WITH_NCCL"), "cudnn": _on("UNDERHFS_WITH_CUDNN")}
+
+
+def _option_flags() -> str:
+    opt = options()
+    return ("" if opt["nccl"] else "-DUHFS_NO_NCCL ") + ("" if opt["cudnn"] else "-DUHFS_NO_CONV ")
+
+
 def _check_flags() -> str:
-    """UNDERHFS_KERNEL_CHECKS=1 compiles the kernels' debug index checks in
+    """Optional debug builds.  UNDERHFS_KERNEL_CHECKS=1 compiles the kernels' debug index checks in
     (UHFS_CHECK in csrc/kernels/common.cuh); a failed check is reported in the
     device status word and the access is skipped, never a trap."""
-    return "-DUHFS_KERNEL_CHECKS " if os.environ.get("UNDERHFS_KERNEL_CHECKS", "0") == "1" else ""
+    flags = "-DUHFS_KERNEL_CHECKS " if os.environ.get("UNDERHFS_KERNEL_CHECKS", "0") == "1" else ""
+    # UNDERHFS_ATTN_TRACE=1: per-step clock64 stamps in the attention kernels
+    # (kernel_cases attn_fwd / attn_bwd --trace); never in the product build
+    if os.environ.get("UNDERHFS_ATTN_TRACE", "0") == "1":
+        flags += "-DUHFS_ATTN_TRACE "
+    return flags + _option_flags()
 
 
 def _pybind11_include() -> str:
@@ -80,9 +113,10 @@ def _ninja_file() -> str:
         f"cxx = {cxx}",
         f"nvflags = {' '.join(ARCH_FLAGS)} -lineinfo -O3 -std=c++17 --expt-relaxed-constexpr {_check_flags()}"
         f"-Xcompiler -fPIC -Xcompiler -fvisibility=hidden -DNDEBUG {incs}",
-        f"cxxflags = -O2 -std=c++17 -fPIC -fvisibility=hidden -DNDEBUG {incs}",
-        f"ldflags = -shared {' '.join(ARCH_FLAGS)} -L{nccl_lib} -l:libnccl.so.2 "
-        f"-Xlinker -rpath,{nccl_lib} -lpthread",
+        f"cxxflags = -O2 -std=c++17 -fPIC -fvisibility=hidden -DNDEBUG {_option_flags()}{incs}",
+        f"ldflags = -shared {' '.join(ARCH_FLAGS)} "
+        + (f"-L{nccl_lib} -l:libnccl.so.2 -Xlinker -rpath,{nccl_lib} " if options()["nccl"] else "")
+        + "-lpthread",
         "rule nvcc",
         "  command = $nvcc $nvflags -MD -MF $out.d -c $in -o $out",
         "  depfile = $out.d",
@@ -120,8 +154,11 @@ def serve_exe_path() -> Path:
     return PKG / "bin" / "underhfs_cpp_serve"
 
 
-def build(verbose: bool = False, jobs: int | None = None) -> Path:
-    """Compile and link the native core; returns the path of the built module."""
+def build(verbose: bool = False, jobs: int | None = None) -> Path | None:
+    """Compile and link the native core; returns the path of the built module
+    (None with UNDERHFS_WITH_CUDA=OFF, which builds nothing)."""
+    if not options()["cuda"]:
+        return None
     BUILD.mkdir(parents=True, exist_ok=True)
     ninja_path = BUILD / "build.ninja"
     content = _ninja_file()

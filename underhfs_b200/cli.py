@@ -83,7 +83,18 @@ TEST_MODULES = [
 
 
 def _cmd_test(_args) -> int:
+    import sys
+    from pathlib import Path
+
     from underhfs_b200.testing import run_test_functions
+
+    # the suite is the source tree's tests/ package: found from the current
+    # directory (an installed console script's sys.path does not include it)
+    # or next to a source checkout of this package
+    for root in (Path.cwd(), Path(__file__).resolve().parents[1]):
+        if (root / "tests" / "__init__.py").exists() and str(root) not in sys.path:
+            sys.path.insert(0, str(root))
+            break
 
     passed = run_test_functions(TEST_MODULES)
     for name in passed:

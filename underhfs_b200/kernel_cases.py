@@ -1,7 +1,7 @@
 """Single-kernel workloads for profiling and micro-benchmarking.
 
     python -m underhfs_b200.kernel_cases <case> [--iters N] [--time]
-    python -m underhfs_b200.kernel_cases {attn_fwd,attn_bwd} --trace
+    UNDERHFS_ATTN_TRACE=1 python -m underhfs_b200._native_build && python -m underhfs_b200.kernel_cases {attn_fwd,attn_bwd} --trace
 
 Each case builds its inputs once, launches one native kernel (or one fused
 op) ``--iters`` times and checks the device status word.  Sizes are chosen
