@@ -50,7 +50,7 @@ CONFIGS = {
     "125m-ddp": dict(model="125m", batch=16, seq=1024, zero=0, desc=MODEL),
     "1.3b-zero2": dict(model="1.3b", batch=8, seq=2048, zero=2,
                        desc="1.3B TransformerLM (d_model 2048, 24 layers, 16 heads, MLP 8192, vocab 32000, tied)"),
-    "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3, offload=True,
+    "7b-zero3": dict(model="7b", batch=2, seq=4096, zero=3,
                      desc="7B TransformerLM (d_model 4096, 32 layers, 32 heads, MLP 11008, vocab 32000, untied)"),
     # the CPU-fallback configuration: the one the reference's own runtime can
     # complete (pure Python, about 2.2-2.5 tokens/s on an 8-core host)
@@ -294,8 +294,11 @@ def run_ours(args) -> int:
             "data": "synthetic uniform token ids in [0,32000) from a fixed seed; random-init weights",
             "config": {"model": cc["desc"], "global_batch": n * cfg.batch, "micro_batch_per_gpu": cfg.batch,
                        "seq_len": cfg.seq_len, "parallelism": f"dp{n}" if cc["zero"] == 0 else f"zero{cc['zero']}-{n}",
-                       "optimizer": ("FusedAdamW lr 3e-4 (fp32 master, one fused launch)" if cc["zero"] == 0 else
-                                     "ZeRO-2 AdamW: fused NVLink reduce-scatter + AdamW + all-gather kernel"),
+                       "optimizer": (f"FusedAdamW lr 3e-4, betas (0.9, 0.95), eps 1e-8, weight decay "
+                                     f"{cfg.weight_decay} (decoupled); fp32 master, one fused launch"
+                                     if cc["zero"] == 0 else
+                                     f"ZeRO-2 AdamW lr 3e-4, betas (0.9, 0.95), weight decay {cfg.weight_decay} "
+                                     "(decoupled): fused NVLink reduce-scatter + AdamW + all-gather kernel"),
                        "grad_allreduce": ("fused NVLink two-shot kernel, 25 MB buckets overlapped with backward"
                                           if cc["zero"] == 0 else "reduce-scatter fused with the AdamW update"),
                        "cuda_graph": not args.no_graph,
@@ -350,9 +353,15 @@ def run_zero3(args, pol, cc) -> int:
     if n > 1:
         init_process_group(pol)
     spec = PRESETS[cc["model"]]
-    offload = cc.get("offload", False) and not args.no_offload
+    # Adam moments: the memory planner decides from this GPU's free memory and
+    # the step's activation estimate (--offload host / device forces it)
+    offload = {"auto": "auto", "host": True, "device": False}[args.offload]
     z = Zero3LM(spec, rank=pol.rank, world=n, device=f"cuda:{local}", lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
-                weight_decay=0.1, decoupled=True, seed=1234, offload_moments=offload)
+                weight_decay=0.1, decoupled=True, seed=1234, offload_moments=offload,
+                activation_bytes=spec.activation_bytes(cc["batch"], cc["seq"]))
+    planner_note = ("" if z.offload_placement is None else
+                    f"; memory planner placed the moments in {z.offload_placement.tier.value} "
+                    f"({z.offload_placement.reason})")
     gen = torch.Generator().manual_seed(1234 + pol.rank)
     pool = [torch.randint(0, spec.vocab_size, (2, cc["batch"], cc["seq"]), generator=gen).cuda() for _ in range(2)]
 
@@ -409,8 +418,10 @@ def run_zero3(args, pol, cc) -> int:
             "data": "synthetic uniform token ids in [0,32000) from a fixed seed; random-init weights",
             "config": {"model": cc["desc"], "global_batch": n * cc["batch"], "micro_batch_per_gpu": cc["batch"],
                        "seq_len": cc["seq"], "parallelism": f"zero3-{n}",
-                       "optimizer": "ZeRO-3 AdamW: per-unit reduce-scatter fused with AdamW on owned rows"
-                                    + ("; Adam moments in pinned host RAM, staged per unit" if offload else ""),
+                       "optimizer": "ZeRO-3 AdamW lr 3e-4, betas (0.9, 0.95), weight decay 0.1 (decoupled): "
+                                    "per-unit reduce-scatter fused with AdamW on owned rows"
+                                    + ("; Adam moments in pinned host RAM, staged per unit" if z.offload
+                                       else "; Adam moments on the device") + planner_note,
                        "param_gather": "per-unit push all-gather over NVLink, prefetched one unit ahead",
                        "cuda_graph": False,
                        "l2": "no flush: per-step working set >> 126 MB L2"},
@@ -434,8 +445,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--no-offload", action="store_true",
-                    help="7b-zero3: keep the Adam moments on the device instead of pinned host RAM")
+    ap.add_argument("--offload", choices=("auto", "host", "device"), default="auto",
+                    help="7b-zero3 Adam moments: the memory planner decides (auto) or force pinned host / device")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="125m-ddp",
                     help="125m-ddp is the headline run; the sharded configurations are measured the same way")
     args = ap.parse_args()

@@ -257,6 +257,58 @@ def case_zero3(rank: int, world: int) -> None:
         z.close()
 
 
+def case_zero3_api(rank: int, world: int) -> None:
+    """ZeRO-3 through the public surface: ZeroAwareAdamW(stage=3) on a
+    TransformerLM (zero_grad / forward / backward / step) and Trainer with
+    zero_stage=3, against the replicated model with FusedAdamW on all-reduced
+    gradients."""
+    from underhfs_b200.nn import TransformerLM
+    from underhfs_b200.optim import FusedAdamW, ZeroAwareAdamW, ZeroShard
+
+    kw = dict(lr=1e-2, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
+    dev = f"cuda:{torch.cuda.current_device()}"
+
+    def model():
+        m = TransformerLM(vocab_size=1024, max_seq_len=256, features=256, hidden_features=1024, layers=2, heads=4,
+                          tied=True, init="normal", seed=9)
+        return m.to(dev, dtype="bf16")
+
+    ref = model()
+    ref_opt = FusedAdamW(ref.parameters(), **kw)
+    m = model()
+    opt = ZeroAwareAdamW(m.parameters(), ZeroShard(rank, world), stage=3, offload="device", **kw)
+    gen = torch.Generator().manual_seed(500 + rank)
+    for _ in range(3):
+        ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+        tg = torch.roll(ids, -1, 1)
+        ref.zero_grad()
+        ref(ids, tg).backward()
+        dist.all_reduce(ref.flat.grads)
+        ref.flat.grads /= world
+        ref_opt.step()
+        opt.zero_grad()
+        m(ids, tg).backward()
+        opt.step()
+    torch.cuda.synchronize()
+    got, want = m.state_dict(as_tensors=True), ref.state_dict(as_tensors=True)
+    for name in want:
+        err = ((got[name] - want[name]).abs().max() / want[name].abs().max().clamp_min(1e-3)).item()
+        assert err < 2e-2, (name, err)
+    opt.zero3.close()
+
+    from underhfs_b200.data import SyntheticTokens
+    from underhfs_b200.distributed import policy_from_env
+    from underhfs_b200.train import TrainConfig, Trainer, build_model
+
+    cfg = TrainConfig(model="125m", batch=2, seq_len=256, zero_stage=3, weight_decay=0.1)
+    tr = Trainer(build_model(cfg, device=dev), cfg, policy=policy_from_env(zero_stage=3))
+    src = SyntheticTokens(32000, cfg.batch, cfg.seq_len, seed=3, rank=rank)
+    host = torch.empty((2, cfg.batch, cfg.seq_len), dtype=torch.int64, pin_memory=True)
+    losses = [tr.step_from_host(src.next_host(host)) for _ in range(4)]
+    tr.release()
+    assert all(l == l for l in losses) and losses[-1] < losses[0], losses
+
+
 def case_native(rank: int, world: int) -> None:
     """The reference-style native NCCL group (host lists and device pointers),
     bootstrapped through UNDERHFS_NCCL_UNIQUE_ID or the torch store."""
@@ -326,7 +378,7 @@ def main() -> int:
     case = sys.argv[1]
     rank, world = _setup()
     try:
-        cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3,
+        cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3, "zero3_api": case_zero3_api,
                  "native": case_native, "cp": case_cp, "nvls": case_nvls}
         cases[case](rank, world)
         dist.barrier()

@@ -132,26 +132,43 @@ def _cmd_train(args) -> int:
     from underhfs_b200.train import TrainConfig, Trainer, build_model
 
     cfg = TrainConfig(model=args.model, batch=args.batch, seq_len=args.seq_len_train, lr=args.lr_train,
-                      zero_stage=args.zero, cuda_graph=not args.no_graph,
+                      zero_stage=args.zero, cuda_graph=not args.no_graph, offload=args.offload,
                       context_parallel=getattr(args, "context_parallel", False))
     from underhfs_b200.distributed import policy_from_env
+    from underhfs_b200.train import StepMeter
 
     pol = policy_from_env(zero_stage=cfg.zero_stage)
     if pol.world_size > 1:
         torch.cuda.set_device(pol.local_rank or 0)
     model = build_model(cfg, device=f"cuda:{pol.local_rank or 0}")
+    spec = model.spec
     trainer = Trainer(model, cfg, policy=pol)
     # context parallelism: every rank draws the same sequences and trains on its shard
     data = SyntheticTokens(model.vocab_size, cfg.batch, cfg.seq_len, seed=cfg.seed,
                            rank=0 if cfg.context_parallel else pol.rank)
     host = torch.empty((2, cfg.batch, cfg.seq_len), dtype=torch.int64, pin_memory=True)
-    losses = []
-    for _ in range(args.steps):
+    tokens_per_step = cfg.batch * (cfg.seq_len if not cfg.context_parallel else cfg.seq_len // pol.world_size)
+    meter = StepMeter(world=pol.world_size, tokens_per_rank=tokens_per_step,
+                      flops_per_token=spec.train_flops_per_token(cfg.seq_len), peak_tflops=args.peak_tflops)
+    losses, records = [], []
+    for i in range(args.steps):
+        meter.start()
         losses.append(trainer.step_from_host(data.next_host(host)))
+        rec = meter.stop()  # device time of this step, max over ranks (a collective)
+        rec.update(step=i, loss=losses[-1])
+        records.append(rec)
+        if pol.rank == 0 and args.log_every and (i % args.log_every == 0 or i == args.steps - 1):
+            print(json.dumps(rec), flush=True)
     trainer.release()
     if pol.rank == 0:
+        timed = records[1:] or records  # the first step includes capture / warm-up
         print(json.dumps({"mode": "train", "model": args.model, "world_size": pol.world_size, "steps": args.steps,
-                          "initial_loss": losses[0], "final_loss": losses[-1], "losses": losses}, indent=2))
+                          "zero_stage": cfg.zero_stage, "initial_loss": losses[0], "final_loss": losses[-1],
+                          "losses": losses,
+                          "tokens_per_s": sum(r["tokens_per_s"] for r in timed) / len(timed),
+                          "max_memory_gb": max(r["max_memory_gb"] for r in records),
+                          "mfu": sum(r["mfu"] for r in timed) / len(timed),
+                          "peak_tflops": args.peak_tflops}, indent=2))
     return 0
 
 
@@ -289,8 +306,13 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--batch", type=int, default=16)
     p.add_argument("--seq-len-train", type=int, default=1024)
     p.add_argument("--lr-train", type=float, default=3e-4)
-    p.add_argument("--zero", type=int, default=0)
+    p.add_argument("--zero", type=int, default=0, choices=(0, 1, 2, 3))
+    p.add_argument("--offload", choices=("auto", "host", "device"), default="auto",
+                   help="ZeRO-3 Adam moments: the memory planner decides (auto), or force pinned host / device")
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--log-every", type=int, default=1, help="print a per-step JSON record every N steps (0: off)")
+    p.add_argument("--peak-tflops", type=float, default=2250.0,
+                   help="bf16 dense peak per GPU for the MFU column (default: B200 nominal 2250)")
     p.add_argument("--context-parallel", action="store_true",
                    help="shard every sequence over all ranks (zigzag) instead of giving each rank its own batch")
     p.set_defaults(func=_cmd_train)

@@ -60,6 +60,17 @@ class LMSpec:
             n += V * F
         return n
 
+    def activation_bytes(self, batch: int, seq_len: int) -> int:
+        """Device bytes the engine keeps for one training step's backward:
+        per token and block the bf16 tensors saved by the forward (x, rmsnorm
+        out, qkv, attention out, x1, rmsnorm out: 8F; fc1 pre- and
+        post-activation: 2 x hidden) plus the bf16 logits / logits gradient and
+        a transient of two blocks' worth of gradients of the activations."""
+        tokens = batch * seq_len
+        per_block = 2 * (8 * self.features + 2 * self.hidden_features)
+        transient = 2 * 2 * (4 * self.features + self.hidden_features)
+        return int(tokens * (self.layers * per_block + 2 * self.vocab_size + transient))
+
     def train_flops_per_token(self, seq_len: int) -> float:
         """6N for the dense weights + causal attention (fwd 2 matmuls, bwd 4)."""
         dense = 6.0 * (self.num_params() - self.vocab_size * self.features - self.max_seq_len * self.features)

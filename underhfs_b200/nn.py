@@ -467,6 +467,7 @@ class TransformerLM(Module):
             self.head = Linear(features, vocab_size, bias=False)
         object.__setattr__(self, "_engine", None)
         object.__setattr__(self, "_flat", None)
+        object.__setattr__(self, "_zero3", None)
         if init != "reference":
             self._reinit(init, seed)
 
@@ -490,6 +491,9 @@ class TransformerLM(Module):
 
     def to(self, device: Device | str | None = None, dtype: DType | str | None = None,
            *, grad_alloc=None) -> "TransformerLM":
+        if self._zero3 is not None:
+            raise RuntimeError("this TransformerLM is sharded by ZeRO-3; its parameters live in the shards "
+                               "(use state_dict() to gather them)")
         target = self.token_embedding.weight.device if device is None else Device.parse(device)
         want = DType(dtype) if dtype is not None else self.token_embedding.weight.dtype
         if target.kind == "cuda" and want is DType.BF16 and self.features // self.heads in (64, 128):
@@ -517,6 +521,7 @@ class TransformerLM(Module):
             object.__setattr__(p, "_flat", flat)
         anchor = torch.zeros((), device=device.torch(), requires_grad=True)
         flat.rehome = self.rehome_buffers
+        flat.owner = self
         object.__setattr__(self, "_flat", flat)
         object.__setattr__(self, "_anchor", anchor)
         object.__setattr__(self, "_engine", LMEngine(spec, flat))
@@ -548,6 +553,48 @@ class TransformerLM(Module):
             engine.positions = old.positions
         object.__setattr__(self, "_engine", engine)
 
+    def attach_zero3(self, zero3) -> None:
+        """Hand this model to a ZeRO-3 sharded runtime (parallel.zero3.Zero3LM,
+        built by ``ZeroAwareAdamW(..., stage=3)``): forward / backward run on its
+        engine, which gathers each unit's weights before use, and the full
+        flat buffers are released, so the rank keeps only its shard.  The
+        parameters become shape-only placeholders (meta tensors);
+        ``state_dict()`` / ``load_state_dict()`` gather / scatter through the
+        shards (collectives: call them on every rank)."""
+        object.__setattr__(self, "_zero3", zero3)
+        object.__setattr__(self, "_engine", zero3.engine)
+        object.__setattr__(self, "_flat", None)
+        for _, p in self.named_parameters():
+            p._data = torch.empty(p.shape, dtype=torch.bfloat16, device="meta")
+            for attr in ("_main_grad", "_master", "_flat"):
+                if hasattr(p, attr):
+                    object.__setattr__(p, attr, None)
+
+    @property
+    def zero3(self):
+        return self._zero3
+
+    def _engine_device(self) -> torch.device:
+        return self._zero3.device if self._zero3 is not None else self._flat.device
+
+    def state_dict(self, *, as_tensors: bool = False) -> dict[str, Any]:
+        if self._zero3 is None:
+            return super().state_dict(as_tensors=as_tensors)
+        full = self._zero3.full_state()  # all-gather of every shard (fp32, CPU)
+        return {name: (full[name].clone() if as_tensors else full[name].double().tolist())
+                for name, _ in self.named_parameters()}
+
+    def load_state_dict(self, state: dict[str, Any]) -> None:
+        if self._zero3 is None:
+            return super().load_state_dict(state)
+        full = {}
+        for name, p in self.named_parameters():
+            if name not in state:
+                raise KeyError(f"missing parameter {name}")
+            value = state[name]._data if isinstance(state[name], Tensor) else state[name]
+            full[name] = (value if isinstance(value, torch.Tensor) else torch.tensor(value)).reshape(p.shape)
+        self._zero3.load_full_state(full)
+
     @property
     def engine(self):
         return self._engine
@@ -557,6 +604,8 @@ class TransformerLM(Module):
         return self._flat
 
     def zero_grad(self) -> None:
+        if self._zero3 is not None:
+            return  # ZeRO-3 clears each unit's gradient slot as its backward begins
         if self._flat is not None:
             self._flat.zero_grad()
         else:
@@ -590,7 +639,7 @@ class TransformerLM(Module):
         return F.cross_entropy(logits.reshape(-1, self.vocab_size), Tensor._wrap(tg.reshape(-1)))
 
     def _engine_forward(self, ids: torch.Tensor, targets) -> Tensor:
-        dev = self._flat.device
+        dev = self._engine_device()
         batched = ids.dim() == 2
         ids2 = (ids if batched else ids.unsqueeze(0)).to(dev, torch.int64)
         like = self.token_embedding.weight
@@ -621,7 +670,8 @@ class TransformerLM(Module):
         with torch.no_grad():
             for _ in range(max_new_tokens):
                 context = generated[-self.max_seq_len:]
-                dev = self._flat.device if self._flat is not None else self.token_embedding.weight._data.device
+                dev = (self._engine_device() if self._engine is not None
+                       else self.token_embedding.weight._data.device)
                 logits = self(torch.tensor(context, dtype=torch.int64, device=dev))
                 generated.append(int(torch.argmax(logits._data[-1].float()).item()))
         return tensor(generated)

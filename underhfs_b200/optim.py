@@ -320,41 +320,97 @@ class ZeroShard:
 
 
 class ZeroAwareAdamW(AdamW):
-    """AdamW whose state is partitioned across data-parallel ranks.
+    """AdamW whose state is partitioned across data-parallel ranks
+    (the reference's surface: ``ZeroAwareAdamW(params, shard=ZeroShard(...))``,
+    optim.py:216-225 of the reference, where it is a single-process stub).
 
     ``stage`` 1/2: master weights and moments are held for the local 1/W
     shard only; ``step()`` runs the fused reduce-scatter + AdamW + all-gather
-    kernel.  Stage 3 additionally keeps only the local shard of the bf16
-    parameters resident (the engine gathers each layer's weights before use).
-    With world_size == 1 it behaves exactly like AdamW.
+    kernel.
+
+    ``stage`` 3: the parameters of a TransformerLM on the CUDA engine are
+    sharded too.  Construction builds the ZeRO-3 runtime
+    (parallel.zero3.Zero3LM) from the model's current weights and attaches it
+    to the model: every rank keeps 1/W of the bf16 weights, fp32 master and
+    moments; forward gathers each unit's weights just before use (the gather
+    fused into the first GEMM that reads them) and backward reduces each
+    unit's gradients with a kernel that applies the AdamW update to the owned
+    rows as it goes.  ``step()`` therefore only closes the step; call it after
+    every backward (no gradient accumulation at stage 3).  ``offload`` places
+    the Adam moments: ``"auto"`` (default) asks the memory planner, which
+    keeps them in device memory when they fit next to the step's other
+    buffers and ``activation_bytes``, else pinned host RAM; ``"host"`` /
+    ``"device"`` force it.  ``world_size == 1`` is allowed at every stage.
     """
 
     def __init__(self, params: Iterable[Tensor], shard: ZeroShard | None = None, *, stage: int = 2,
-                 group=None, **kwargs) -> None:
+                 group=None, offload: str = "auto", planner=None, activation_bytes: int = 0,
+                 **kwargs) -> None:
         params = list(params)
         self.shard = shard or ZeroShard()
         self.stage = stage
+        if stage not in (1, 2, 3):
+            raise ValueError("ZeRO stage must be 1, 2 or 3")
         self._zero = None
+        self._zero3 = None
         flat = _shared_flat(params)
-        if self.shard.world_size > 1 and flat is not None:
+        if stage == 3:
+            self._set_hparams(params, kwargs)
+            self._init_stage3(flat, group, offload, planner, activation_bytes)
+        elif self.shard.world_size > 1 and flat is not None:
             from underhfs_b200.parallel.zero import ZeroFlatOptimizer
 
-            Optimizer.__init__(self, params)
-            betas = kwargs.get("betas", (0.9, 0.999))
-            if not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
-                raise ValueError("AdamW betas must be in the range [0, 1)")
-            self.lr = kwargs.get("lr", 1e-3)
-            self.betas = tuple(betas)
-            self.eps = kwargs.get("eps", 1e-8)
-            self.weight_decay = kwargs.get("weight_decay", 0.01)
-            self.decoupled = kwargs.get("decoupled", False)
-            self.step_count = 0
+            self._set_hparams(params, kwargs)
             self._flat = flat
             self._zero = ZeroFlatOptimizer(flat, self.shard, group=group, stage=stage)
         else:
             super().__init__(params, **kwargs)
 
+    def _set_hparams(self, params: list, kwargs: dict) -> None:
+        Optimizer.__init__(self, params)
+        betas = kwargs.get("betas", (0.9, 0.999))
+        if not 0 <= betas[0] < 1 or not 0 <= betas[1] < 1:
+            raise ValueError("AdamW betas must be in the range [0, 1)")
+        self.lr = kwargs.get("lr", 1e-3)
+        self.betas = tuple(betas)
+        self.eps = kwargs.get("eps", 1e-8)
+        self.weight_decay = kwargs.get("weight_decay", 0.01)
+        self.decoupled = kwargs.get("decoupled", False)
+        self.step_count = 0
+        self._flat = None
+
+    def _init_stage3(self, flat, group, offload: str, planner, activation_bytes: int) -> None:
+        model = getattr(flat, "owner", None) if flat is not None else None
+        if model is None or not hasattr(model, "attach_zero3"):
+            raise ValueError("ZeRO stage 3 shards a TransformerLM on the CUDA engine: pass the parameters of a "
+                             "TransformerLM moved with .to('cuda', dtype='bf16')")
+        if offload not in ("auto", "host", "device"):
+            raise ValueError("offload must be 'auto', 'host' or 'device'")
+        from underhfs_b200.parallel.zero3 import Zero3LM
+
+        state = {slot.name: (flat.master_view(slot.name) if flat.master is not None else flat.param(slot.name))
+                 .detach().float() for slot in flat.layout.slots}
+        self._zero3 = Zero3LM(
+            model.spec, rank=self.shard.rank, world=self.shard.world_size, device=flat.device, group=group,
+            state=state, lr=self.lr, betas=self.betas, eps=self.eps, weight_decay=self.weight_decay,
+            decoupled=self.decoupled, offload_moments={"auto": "auto", "host": True, "device": False}[offload],
+            planner=planner, activation_bytes=activation_bytes, hparams=self)
+        del state
+        model.attach_zero3(self._zero3)
+
+    @property
+    def zero3(self):
+        return self._zero3
+
+    def zero_grad(self) -> None:
+        if self._zero3 is None:
+            super().zero_grad()
+
     def step(self) -> None:
+        if self._zero3 is not None:
+            self.step_count += 1
+            self._zero3.step_done()
+            return
         if self._zero is None:
             super().step()
             return
@@ -363,17 +419,23 @@ class ZeroAwareAdamW(AdamW):
                         decoupled=self.decoupled)
 
     def step_split(self, boundary: int, wait) -> None:
-        if self._zero is None:
+        if self._zero is None and self._zero3 is None:
             super().step_split(boundary, wait)
             return
         wait()  # the sharded update reduces every gradient itself
         self.step()
 
     def state_dict(self) -> dict:
-        if self._zero is None:
+        if self._zero is None and self._zero3 is None:
             return super().state_dict()
-        return {"step_count": self.step_count, "lr": self.lr, "betas": list(self.betas), "eps": self.eps,
-                "weight_decay": self.weight_decay, "zero": self._zero.shard_state()}
+        out = {"step_count": self.step_count, "lr": self.lr, "betas": list(self.betas), "eps": self.eps,
+               "weight_decay": self.weight_decay}
+        if self._zero is not None:
+            out["zero"] = self._zero.shard_state()
+        else:
+            out["zero3"] = {"stage": 3, "rank": self.shard.rank, "world_size": self.shard.world_size,
+                            "moments_offloaded": bool(self._zero3.offload)}
+        return out
 
 
 _ = DType  # re-exported for callers that type-annotate with the optimizer module

@@ -23,7 +23,11 @@ The two slots of the block ring are reused every second block; the gather
 and reduce kernels open and close with a cross-rank barrier, so no rank
 overwrites a slot a peer is still reading.
 
-Moment offload (``offload_moments=True``): the fp32 Adam moments of the shard
+Moment offload: with ``offload_moments="auto"`` the memory planner
+(runtime.MemoryPlanner.place_optimizer_state) decides from this GPU's free
+memory, less the step's activation estimate, whether the two fp32 moments of
+the shard stay in device memory or go to pinned host RAM; ``True`` / ``False``
+force the choice.  Offloaded, the fp32 Adam moments of the shard
 live in pinned host RAM.  A unit's moments (a contiguous shard range) are
 copied into one of two device staging slots on a copy stream when the unit's
 backward begins, the fused reduce-scatter + AdamW kernel updates them there,
@@ -140,11 +144,16 @@ class Zero3LM:
                  group=None, init: str = "normal", seed: int = 0, state: dict | None = None,
                  lr: float = 3e-4, betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, decoupled: bool = True, blocks: int = 128,
-                 overlap: bool = True, fused_gather: bool = True, offload_moments: bool = False) -> None:
+                 overlap: bool = True, fused_gather: bool = True, offload_moments: bool | str = False,
+                 planner=None, activation_bytes: int = 0, hparams=None) -> None:
         self.spec = spec
         self.overlap = overlap
-        self.offload = offload_moments
         self.fused = fused_gather
+        # hparams: an object with lr / betas / eps / weight_decay / decoupled
+        # (the optimizer that owns this runtime) read at every update, so
+        # schedule changes on the optimizer take effect
+        self.hparams = hparams
+        self._await_step = False
         self.rank, self.world = rank, world
         self.device = torch.device(device)
         self.lr, self.betas, self.eps = lr, betas, eps
@@ -154,6 +163,22 @@ class Zero3LM:
         self.by_name = {s.name: s for s in self.layout.slots}
         self.units: dict = {}
         self._build_units()
+        self.offload_placement = None
+        if offload_moments == "auto":
+            from underhfs_b200.runtime import MemoryPlanner
+
+            planner = planner or MemoryPlanner.for_device(self.device)
+            # resident besides the moments: bf16 shard + fp32 master, the gather
+            # and gradient slots (embed, tail, two blocks; 6 bytes per element)
+            slots = (self.units["embed"].size + self.units["tail"].size
+                     + 2 * max((self.units[i].size for i in range(spec.layers)), default=0))
+            resident = 6 * self.shard_total + 6 * slots
+            self.offload_placement = planner.place_optimizer_state(
+                8 * self.shard_total, device_headroom=resident + int(activation_bytes))
+            from underhfs_b200.cuda import MemoryTier
+
+            offload_moments = self.offload_placement.tier is not MemoryTier.VRAM
+        self.offload = bool(offload_moments)
         # shard storage (this rank's rows of every parameter)
         n = self.shard_total
         self.shard16 = torch.zeros(n, dtype=torch.bfloat16, device=self.device)
@@ -477,6 +502,11 @@ class Zero3LM:
         if self.offload:
             self._stage_moments(key)
         if key == "tail":
+            if self.hparams is not None:
+                if self._await_step:
+                    raise RuntimeError("ZeRO-3 applies the AdamW update inside backward(): call optimizer.step() "
+                                       "after every backward (gradient accumulation is not available at stage 3)")
+                self._await_step = True
             K.increment_(self.step_t)
             # the head gradient of a tied model lands in the embedding unit
             off = self.slot_off["embed"]
@@ -501,6 +531,7 @@ class Zero3LM:
             self._reduce_impl(key)
 
     def _reduce_impl(self, key) -> None:
+        hp = self.hparams if self.hparams is not None else self
         u = self.units[key]
         slot = self._slot_key(key)
         if self.overlap:
@@ -516,8 +547,8 @@ class Zero3LM:
             m_ptr, v_ptr = self.m.data_ptr(), self.v.data_ptr()
         core().comm_rs_adamw_segments(
             self.gradsym.heap, self.slot_off[slot] * 4, self._segs(u), self.master.data_ptr(), m_ptr,
-            v_ptr, self.shard16.data_ptr(), float(self.lr), float(self.betas[0]), float(self.betas[1]),
-            float(self.eps), float(self.weight_decay), float(1.0 / self.world), bool(self.decoupled),
+            v_ptr, self.shard16.data_ptr(), float(hp.lr), float(hp.betas[0]), float(hp.betas[1]),
+            float(hp.eps), float(hp.weight_decay), float(1.0 / self.world), bool(hp.decoupled),
             self.step_t.data_ptr(), self.nblocks, stream)
         if self.offload:
             self._unstage_moments(key, mslot, run)
@@ -547,9 +578,23 @@ class Zero3LM:
             for s, (nat, soff, ln) in zip(u.slots, u.segs):
                 part = self.master[soff: soff + ln].contiguous()
                 parts = [torch.empty_like(part) for _ in range(W)]
-                dist.all_gather(parts, part)
+                if W > 1:
+                    dist.all_gather(parts, part)
+                else:
+                    parts = [part]
                 out[s.name] = torch.cat(parts).reshape(s.shape).cpu()
         return out
+
+    def step_done(self) -> None:
+        """The owning optimizer's step(): the update already ran per unit during
+        backward; this closes the step (the next backward may start)."""
+        self._await_step = False
+
+    def load_full_state(self, state: dict) -> None:
+        """Overwrite this rank's shard (fp32 master and bf16 copy) from full
+        parameter tensors keyed by name; moments are kept."""
+        self._init_shards("normal", 0, state)
+        self._gathered.clear()
 
     def close(self) -> None:
         if self.fused:

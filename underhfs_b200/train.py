@@ -46,6 +46,8 @@ class TrainConfig:
     # every rank trains on its zigzag shard of the same sequences (the whole
     # world is one context-parallel group; gradients are averaged by DDP)
     context_parallel: bool = False
+    # ZeRO-3 Adam moments: "auto" (the memory planner decides), "host", "device"
+    offload: str = "auto"
 
 
 def build_model(cfg: TrainConfig, device: str = "cuda"):
@@ -57,6 +59,43 @@ def build_model(cfg: TrainConfig, device: str = "cuda"):
     if device.startswith("cuda"):
         model.to(device, dtype="bf16")
     return model
+
+
+class StepMeter:
+    """Per-step training metrics for logs: device time of the step from CUDA
+    events on the current stream (taken as the max over ranks, a small
+    all-reduce), tokens/s of the whole job, model FLOPs utilisation against
+    ``peak_tflops`` per GPU, and the peak device memory of the step."""
+
+    def __init__(self, *, world: int, tokens_per_rank: int, flops_per_token: float, peak_tflops: float) -> None:
+        self.world = world
+        self.tokens_per_rank = tokens_per_rank
+        self.flops_per_token = flops_per_token
+        self.peak_tflops = peak_tflops
+        self._t0 = self._t1 = None
+
+    def start(self) -> None:
+        torch.cuda.reset_peak_memory_stats()
+        self._t0 = torch.cuda.Event(enable_timing=True)
+        self._t1 = torch.cuda.Event(enable_timing=True)
+        self._t0.record()
+
+    def stop(self) -> dict:
+        self._t1.record()
+        self._t1.synchronize()
+        ms = self._t0.elapsed_time(self._t1)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        tokens = self.tokens_per_rank * self.world
+        tps = tokens / (ms / 1e3)
+        achieved = tps * self.flops_per_token / self.world / 1e12  # TFLOP/s per GPU
+        return {"ms": ms, "tokens_per_s": tps, "tflops_per_gpu": achieved,
+                "mfu": achieved / self.peak_tflops if self.peak_tflops else None,
+                "max_memory_gb": torch.cuda.max_memory_allocated() / 2**30}
 
 
 class Trainer:
@@ -86,13 +125,20 @@ class Trainer:
                 from underhfs_b200.distributed import init_process_group
 
                 init_process_group(self.policy)
+            extra = {}
+            if cfg.zero_stage == 3:
+                # per-unit gathers and reductions synchronise with peers through
+                # flags whose epochs advance on the host: the step stays eager
+                cfg.cuda_graph = False
+                extra = dict(offload=cfg.offload,
+                             activation_bytes=model.spec.activation_bytes(cfg.batch, cfg.seq_len))
             self.opt = ZeroAwareAdamW(model.parameters(), ZeroShard(self.policy.rank, self.world),
                                       stage=cfg.zero_stage, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
-                                      weight_decay=cfg.weight_decay, decoupled=cfg.decoupled)
+                                      weight_decay=cfg.weight_decay, decoupled=cfg.decoupled, **extra)
         else:
             self.opt = FusedAdamW(model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                   weight_decay=cfg.weight_decay, decoupled=cfg.decoupled)
-        dev = model.flat.device
+        dev = model._engine_device()
         local_len = cfg.seq_len // self.world if self.cp is not None else cfg.seq_len
         self.static_ids = torch.zeros((cfg.batch, local_len), dtype=torch.int64, device=dev)
         self.static_tg = torch.zeros_like(self.static_ids)
@@ -192,6 +238,11 @@ class Trainer:
         return float(loss.item())
 
     def release(self) -> None:
-        """Drop the captured graph (before destroying the process group)."""
+        """Drop the captured graph and, at ZeRO stage 3, the sharded runtime's
+        symmetric buffers (before destroying the process group)."""
         self._graph = None
         self._graph_loss = None
+        z = getattr(self.opt, "zero3", None)
+        if z is not None:
+            torch.cuda.synchronize()
+            z.close()
