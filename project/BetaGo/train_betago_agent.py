@@ -1,16 +1,24 @@
-"""BetaGo: a 9x9 Go policy/value network trained on rule-labelled positions.
+"""BetaGo: a 9x9 Go policy/value network trained on labelled positions.
 
-Model (same shape as the reference agent, project/BetaGo/train_betago_agent.py):
-trunk Linear(324,32)-ReLU-Linear(32,16)-ReLU, policy head -> 82 moves (81
-points + pass), value head -> 1.  Loss = cross-entropy(policy) + 0.35 * MSE
-(value), AdamW lr 0.015 wd 1e-4, 60 steps of batch 8.
+Model (same shape as the reference agent, project/BetaGo/train_betago_agent.py
+of the reference): trunk Linear(324,32)-ReLU-Linear(32,16)-ReLU, policy head
+-> 82 moves (81 points + pass), value head -> 1.  Loss = cross-entropy(policy)
++ 0.35 * MSE(value), AdamW lr 0.015 wd 1e-4, 60 steps of batch 8.  Input
+planes: own stones, opponent stones, legal moves, side to move.
 
-Data: positions are produced by a seeded stone scatter plus hand-built tactical
-motifs; the label of each position is the highest-priority move of a tactical
-labeller written for this project (capture, rescue from atari, atari,
-connection, 3-3/4-4 framework, centre), and the value target is the stone
-balance plus the label's tactical weight.  Input planes: own stones, opponent
-stones, legal moves, side to move.
+Two datasets:
+
+* ``task="reference"`` (default): the reference project's supervision task,
+  restated here so the two runtimes train on identical data and their metrics
+  compare -- positions from its seeded scatter generator or its eight
+  strategy motifs (capture, defend-atari, connect, corner framework, side
+  extension, centre influence, atari, shape balance), each labelled with the
+  move of highest score under its tactical / shape heuristic, value target =
+  stone balance + score / 14; 96 training samples, evaluation on samples
+  8..39.  (Task constants are the reference's: train_betago_agent.py:113-251.)
+* ``task="tactical"``: this project's own generator (seeded stone scatter plus
+  hand-built motifs) and priority labeller (capture, rescue, atari, connect,
+  3-3/4-4 framework, centre).
 """
 
 from __future__ import annotations
@@ -196,6 +204,116 @@ def generate_samples(count: int, offset: int = 0) -> list[Sample]:
     return out
 
 
+# ------------------------------------------------- the reference's task
+# Score of a move under the reference labeller: tactical terms from the
+# neighbouring chains (first matching term names the strategy), a positional
+# term, and a small contact term.
+_CHAIN_TERMS = (
+    # (whose chain, liberties the chain has, base score, per-stone bonus, tag)
+    (-1, 1, 9.0, 1.0, "capture"),
+    (-1, 2, 3.0, 0.0, "atari"),
+    (+1, 1, 8.0, 0.5, "defend_atari"),
+)
+_FRAMEWORK_POINTS = {(2, 2), (2, 6), (6, 2), (6, 6)}
+
+
+def reference_score(board, colour: int, move: int) -> tuple[float, str]:
+    if move == PASS:
+        return -1.0, "pass"
+    tags: list[str] = []
+    total = 0.0
+    for q in adjacent(move):
+        if board[q] == 0:
+            continue
+        stones, libs = chain(board, q)
+        if move not in libs:
+            continue
+        side = 1 if board[q] == colour else -1
+        for owner, nlib, base, per_stone, tag in _CHAIN_TERMS:
+            if owner == side and len(libs) == nlib:
+                total += base + per_stone * len(stones)
+                tags.append(tag)
+                break
+        else:
+            if side == 1:  # own chain with two or more liberties: a connection
+                total += 1.8
+                tags.append("connect")
+    r, c = divmod(move, N)
+    edge = min(r, c, N - 1 - r, N - 1 - c)
+    if (r, c) in _FRAMEWORK_POINTS:
+        total += 2.4
+        tags.append("corner_framework")
+    elif edge == 2:
+        total += 1.2
+        tags.append("side_extension")
+    elif 3 <= r <= 5 and 3 <= c <= 5:
+        total += 1.0
+        tags.append("center_influence")
+    own = sum(board[q] == colour for q in adjacent(move))
+    other = sum(board[q] == -colour for q in adjacent(move))
+    total += 0.45 * own + 0.25 * other
+    return total, (tags[0] if tags else "shape_balance")
+
+
+def reference_scatter(seed: int) -> tuple[tuple[int, ...], int]:
+    """Alternating stones placed by the reference's deterministic walk."""
+    b = [0] * POINTS
+    colour, cursor, stride = 1, (seed * 17 + 11) % POINTS, 7 + seed % 5
+    for step in range(10 + seed % 18):
+        for attempt in range(POINTS):
+            p = (cursor + attempt * stride + step * 13) % POINTS
+            if b[p] == 0:
+                b[p] = colour
+                break
+        colour = -colour
+        cursor = (cursor * 19 + 23) % POINTS
+    return tuple(b), (1 if seed % 2 == 0 else -1)
+
+
+# The eight strategy motifs: (move, own stones, opponent stones, tag, score),
+# black to play.
+_MOTIFS = (
+    (40, (49,), (31, 39), "capture", 12.0),
+    (40, (39, 49), (31, 41), "defend_atari", 11.0),
+    (40, (39, 41), (31,), "connect", 8.0),
+    (20, (19,), (11,), "corner_framework", 7.0),
+    (22, (21,), (13,), "side_extension", 6.5),
+    (40, (30, 50), (32, 48), "center_influence", 6.0),
+    (31, (39, 49), (40,), "atari", 7.5),
+    (58, (57, 67), (49,), "shape_balance", 5.5),
+)
+
+
+def reference_samples(count: int) -> list[Sample]:
+    out = []
+    for seed in range(count):
+        motif = _MOTIFS[seed % 8] if seed % 8 < len(_MOTIFS) else None
+        if motif is not None:
+            move, own, opp, tag, score = motif
+            b = [0] * POINTS
+            for q in own:
+                b[q] = 1
+            for q in opp:
+                b[q] = -1
+            board, colour = tuple(b), 1
+        else:
+            board, colour = reference_scatter(seed)
+            ranked = sorted(((reference_score(board, colour, m), m) for m in legal_moves(board, colour)),
+                            key=lambda t: (t[0][0], -t[1]), reverse=True)
+            (score, tag), move = ranked[0]
+        value = max(-1.0, min(1.0, sum(board) * colour / POINTS + score / 14.0))
+        out.append(Sample(encode(board, colour), move, value, tag, board))
+    return out
+
+
+def datasets(task: str) -> tuple[list[Sample], list[Sample]]:
+    if task == "reference":
+        return reference_samples(96), reference_samples(40)[-32:]
+    if task == "tactical":
+        return generate_samples(96), generate_samples(32, offset=1000)
+    raise ValueError("task must be 'reference' or 'tactical'")
+
+
 # ----------------------------------------------------------- training
 def evaluate(model: BetaGoAgent, samples: list[Sample]) -> dict:
     logits, value = model(tensor([s.features for s in samples]))
@@ -217,9 +335,8 @@ def evaluate(model: BetaGoAgent, samples: list[Sample]) -> dict:
             "strategy_accuracy": {k: w / t for k, (w, t) in sorted(per.items())}}
 
 
-def train(*, steps: int = 60, batch_size: int = 8, write_artifacts: bool = True) -> dict:
-    train_set = generate_samples(96)
-    eval_set = generate_samples(32, offset=1000)
+def train(*, steps: int = 60, batch_size: int = 8, write_artifacts: bool = True, task: str = "reference") -> dict:
+    train_set, eval_set = datasets(task)
     model = BetaGoAgent()
     opt = AdamW(model.parameters(), lr=0.015, weight_decay=1e-4)
     history = []
@@ -234,7 +351,8 @@ def train(*, steps: int = 60, batch_size: int = 8, write_artifacts: bool = True)
         if step % 10 == 0 or step == steps - 1:
             history.append({**evaluate(model, eval_set), "step": step, "loss": loss.item()})
     final = evaluate(model, eval_set)
-    payload = {"board_size": N, "train_samples": len(train_set), "eval_samples": len(eval_set), "steps": steps,
+    payload = {"task": task, "board_size": N, "train_samples": len(train_set), "eval_samples": len(eval_set),
+               "steps": steps,
                "batch_size": batch_size, "final_metrics": final, "history": history,
                "strategies": sorted({s.strategy for s in train_set})}
     if write_artifacts:
@@ -243,15 +361,15 @@ def train(*, steps: int = 60, batch_size: int = 8, write_artifacts: bool = True)
         state_path = art / "betago_agent_state.json"
         save_checkpoint(state_path, state=model.state_dict(),
                         metadata={"board_size": N, "features": FEATURES, "moves": POINTS + 1,
-                                  "training": "rule-labelled tactical positions"})
+                                  "training": f"{task} strategy supervision"})
         payload["artifact"] = str(state_path.relative_to(HERE.parents[1]))
         (art / "metrics.json").write_text(json.dumps(payload, indent=2), encoding="utf-8")
     return payload
 
 
-def run_smoke(*, steps: int = 5) -> dict:
-    return train(steps=steps, write_artifacts=False)
+def run_smoke(*, steps: int = 5, task: str = "reference") -> dict:
+    return train(steps=steps, write_artifacts=False, task=task)
 
 
 if __name__ == "__main__":
-    print(json.dumps(train(), indent=2))
+    print(json.dumps(train(task=sys.argv[1] if len(sys.argv) > 1 else "reference"), indent=2))

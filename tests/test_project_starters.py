@@ -71,3 +71,22 @@ def test_betago_smoke():
     assert r["final_metrics"]["value_mae"] >= 0.0
     board = tuple([0] * mod.POINTS)
     assert len(mod.legal_moves(board, 1)) == mod.POINTS
+
+
+def test_betago_reference_task_reproduces_published_metrics():
+    """The reference project's own BetaGo task, trained with this framework's
+    Linear / AdamW / losses (CPU, fp64), lands on the metrics the reference
+    publishes in project/BetaGo/artifacts/metrics.json: top-1 0.500, top-3
+    0.875, value MAE 0.236 (0.23625455480191412), final loss 1.1061586872606768."""
+    mod = _load("project/BetaGo/train_betago_agent.py")
+    r = mod.train(write_artifacts=False, task="reference")
+    m = r["final_metrics"]
+    assert m["policy_top1"] == 0.5 and m["policy_top3"] == 0.875
+    assert abs(m["value_mae"] - 0.23625455480191412) < 1e-9
+    assert abs(r["history"][-1]["loss"] - 1.1061586872606768) < 1e-9
+
+
+def test_betago_tactical_task_still_trains():
+    mod = _load("project/BetaGo/train_betago_agent.py")
+    r = mod.run_smoke(steps=3, task="tactical")
+    assert r["task"] == "tactical" and 0.0 <= r["final_metrics"]["policy_top1"] <= 1.0

@@ -160,6 +160,19 @@ def initial_value(spec: LMSpec, name: str, shape: tuple[int, ...], init: str, ge
     return torch.randn(shape, generator=gen) * std
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    """One side stream per device for work that runs beside the backward."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(key)
+    if st is None:
+        st = _SIDE_STREAMS[key] = torch.cuda.Stream(device=torch.device("cuda", key))
+    return st
+
+
 class LMEngine:
     """Forward/backward of one TransformerLM over flat buffers, on the current stream."""
 
@@ -330,40 +343,61 @@ class LMEngine:
         elif hook is not None:
             hook(self.flat.by_name["norm.weight"].offset, self.flat.numel)
         del dl, dhf
+        # Bias gradients are column sums of the output gradients: HBM-bound
+        # reductions launched on a side stream as soon as their input exists,
+        # so they run beside the compute-bound GEMMs of the same block; the
+        # compute stream joins the side stream at the end of the block (before
+        # the block's gradients are handed to the reduction hooks).
+        flat = getattr(self, "flat", None)
+        side = _side_stream(flat.device if flat is not None else None)
+        pending: list = []
+
+        def colsum_async(x, out):
+            if out is None:
+                return
+            ready = torch.cuda.Event()
+            ready.record()
+            side.wait_event(ready)
+            with torch.cuda.stream(side):
+                K.colsum_accum(x, out)
+            pending.append(x)  # kept alive until the join
+
+        def join():
+            if pending:
+                torch.cuda.current_stream().wait_stream(side)
+                pending.clear()
+
         for bi in range(len(self.blocks) - 1, -1, -1):
             blk, saved = self.blocks[bi], sv["blocks"][bi]
             nvtx.push(f"bwd/block{bi}")
             self.unit_backward_begin(bi)
             x, h1, r1, qkv, o, lse, x1, h2, r2, u, g = saved
             # MLP
+            colsum_async(dx, blk["gb2"])
             du = K.linear_dgrad(dx, blk["W2"], gelu_in=u)
             K.linear_wgrad_accum(dx, g, blk["gW2"])
-            if blk["gb2"] is not None:
-                K.colsum_accum(dx, blk["gb2"])
+            colsum_async(du, blk["gb1"])
             dh2 = K.linear_dgrad(du, blk["W1"])
             K.linear_wgrad_accum(du, h2, blk["gW1"])
-            if blk["gb1"] is not None:
-                K.colsum_accum(du, blk["gb1"])
             del du
             dx1 = K.rmsnorm_backward(dh2, x1, blk["ln2"], r2, dx, blk["g_ln2"])
             del dh2
             # attention
+            colsum_async(dx1, blk["gbo"])
             do = K.linear_dgrad(dx1, blk["Wo"])
             K.linear_wgrad_accum(dx1, o, blk["gWo"])
-            if blk["gbo"] is not None:
-                K.colsum_accum(dx1, blk["gbo"])
             if self.context_attention is not None:
                 dqkv = self.context_attention.backward(qkv, o, lse, do, B, T, H, D)
             else:
                 dqkv = K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, self.causal)
             del do
+            colsum_async(dqkv, blk["gbqkv"])
             dh1 = K.linear_dgrad(dqkv, blk["Wqkv"])
             K.linear_wgrad_accum(dqkv, h1, blk["gWqkv"])
-            if blk["gbqkv"] is not None:
-                K.colsum_accum(dqkv, blk["gbqkv"])
             del dqkv
             dx = K.rmsnorm_backward(dh1, x, blk["ln1"], r1, dx1, blk["g_ln1"])
             del dh1, dx1
+            join()
             self.unit_backward_end(bi)
             if hook is not None:
                 hook(*blk["range"])
