@@ -4,9 +4,7 @@
 //   * single-head fp32 attention (reference cuda_attention_f32,
 //     cuda/kernels.cu:147-188 — there O(T^2 F^2); here each score is computed
 //     once per (query, key) in shared memory);
-//   * conv2d forward / data-gradient / weight-gradient (reference: cuDNN
-//     calls at cuda/kernels.cu:1093-1115, 1252-1265, 1395-1408) as direct
-//     convolutions in fp32.
+//   (conv2d forward / data-gradient / weight-gradient: conv_igemm.cu.)
 // These serve the small fp32 API surface; the bf16 training path uses the
 // tcgen05 GEMM and the flash-attention kernels.
 #include <stdexcept>
@@ -118,99 +116,6 @@ __global__ void attention_f32_kernel(const float* __restrict__ q, const float* _
   }
 }
 
-__global__ void conv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                const float* __restrict__ b, float* __restrict__ y, int N, int C, int H, int W, int K,
-                                int R, int S, int sh, int sw, int ph, int pw, int P, int Q) {
-  const long long total = (long long)N * K * P * Q;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    int q = idx % Q;
-    int p = (idx / Q) % P;
-    int kk = (idx / ((long long)P * Q)) % K;
-    int n = idx / ((long long)K * P * Q);
-    float acc = b != nullptr ? b[kk] : 0.f;
-    for (int c = 0; c < C; ++c)
-      for (int r = 0; r < R; ++r) {
-        int ih = p * sh + r - ph;
-        if (ih < 0 || ih >= H) continue;
-        for (int s = 0; s < S; ++s) {
-          int iw = q * sw + s - pw;
-          if (iw < 0 || iw >= W) continue;
-          acc += x[(((long long)n * C + c) * H + ih) * W + iw] * w[(((long long)kk * C + c) * R + r) * S + s];
-        }
-      }
-    y[idx] = acc;
-  }
-}
-
-__global__ void conv_dgrad_kernel(const float* __restrict__ dy, const float* __restrict__ w, float* __restrict__ dx,
-                                  int N, int C, int H, int W, int K, int R, int S, int sh, int sw, int ph, int pw,
-                                  int P, int Q) {
-  const long long total = (long long)N * C * H * W;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    int iw = idx % W;
-    int ih = (idx / W) % H;
-    int c = (idx / ((long long)H * W)) % C;
-    int n = idx / ((long long)C * H * W);
-    float acc = 0.f;
-    for (int kk = 0; kk < K; ++kk)
-      for (int r = 0; r < R; ++r) {
-        int t = ih + ph - r;
-        if (t < 0 || t % sh != 0) continue;
-        int p = t / sh;
-        if (p >= P) continue;
-        for (int s = 0; s < S; ++s) {
-          int u = iw + pw - s;
-          if (u < 0 || u % sw != 0) continue;
-          int q = u / sw;
-          if (q >= Q) continue;
-          acc += dy[(((long long)n * K + kk) * P + p) * Q + q] * w[(((long long)kk * C + c) * R + r) * S + s];
-        }
-      }
-    dx[idx] = acc;
-  }
-}
-
-__global__ void conv_wgrad_kernel(const float* __restrict__ dy, const float* __restrict__ x, float* __restrict__ dw,
-                                  float* __restrict__ db, int N, int C, int H, int W, int K, int R, int S, int sh,
-                                  int sw, int ph, int pw, int P, int Q) {
-  const long long total = (long long)K * C * R * S;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    int s = idx % S;
-    int r = (idx / S) % R;
-    int c = (idx / ((long long)R * S)) % C;
-    int kk = idx / ((long long)C * R * S);
-    float acc = 0.f;
-    for (int n = 0; n < N; ++n)
-      for (int p = 0; p < P; ++p) {
-        int ih = p * sh + r - ph;
-        if (ih < 0 || ih >= H) continue;
-        for (int q = 0; q < Q; ++q) {
-          int iw = q * sw + s - pw;
-          if (iw < 0 || iw >= W) continue;
-          acc += dy[(((long long)n * K + kk) * P + p) * Q + q] * x[(((long long)n * C + c) * H + ih) * W + iw];
-        }
-      }
-    dw[idx] = acc;
-  }
-  if (db != nullptr) {
-    for (long long kk = blockIdx.x * (long long)blockDim.x + threadIdx.x; kk < K;
-         kk += (long long)gridDim.x * blockDim.x) {
-      float acc = 0.f;
-      for (int n = 0; n < N; ++n)
-        for (int pq = 0; pq < P * Q; ++pq) acc += dy[((long long)n * K + kk) * P * Q + pq];
-      db[kk] = acc;
-    }
-  }
-}
-
-int flat_grid(long long total) {
-  long long g = (total + 255) / 256;
-  if (g > 148LL * 8) g = 148LL * 8;
-  return (int)(g < 1 ? 1 : g);
-}
 
 }  // namespace
 
@@ -230,30 +135,6 @@ void attention_naive_f32(const float* q, const float* k, const float* v, float* 
     UHFS_CUDA_CHECK(cudaFuncSetAttribute(attention_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          tokens * (int)sizeof(float)));
   attention_f32_kernel<<<tokens, 128, tokens * sizeof(float), s>>>(q, k, v, out, tokens, features, scale, causal);
-  note_launch();
-  UHFS_CUDA_CHECK(cudaGetLastError());
-}
-
-void conv2d_fwd_f32(const float* x, const float* w, const float* b, float* y, int N, int C, int H, int W, int K,
-                    int R, int S, int sh, int sw, int ph, int pw, int P, int Q, cudaStream_t s) {
-  conv_fwd_kernel<<<flat_grid((long long)N * K * P * Q), 256, 0, s>>>(x, w, b, y, N, C, H, W, K, R, S, sh, sw, ph, pw,
-                                                                      P, Q);
-  note_launch();
-  UHFS_CUDA_CHECK(cudaGetLastError());
-}
-
-void conv2d_dgrad_f32(const float* dy, const float* w, float* dx, int N, int C, int H, int W, int K, int R, int S,
-                      int sh, int sw, int ph, int pw, int P, int Q, cudaStream_t s) {
-  conv_dgrad_kernel<<<flat_grid((long long)N * C * H * W), 256, 0, s>>>(dy, w, dx, N, C, H, W, K, R, S, sh, sw, ph, pw,
-                                                                        P, Q);
-  note_launch();
-  UHFS_CUDA_CHECK(cudaGetLastError());
-}
-
-void conv2d_wgrad_f32(const float* dy, const float* x, float* dw, float* db, int N, int C, int H, int W, int K,
-                      int R, int S, int sh, int sw, int ph, int pw, int P, int Q, cudaStream_t s) {
-  conv_wgrad_kernel<<<flat_grid((long long)K * C * R * S), 256, 0, s>>>(dy, x, dw, db, N, C, H, W, K, R, S, sh, sw, ph,
-                                                                        pw, P, Q);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }

@@ -316,3 +316,34 @@ def test_out_of_range_ids_and_targets_are_reported_not_read(K):
     assert K.core().device_status(True)["code"] == 5
     assert torch.isfinite(loss[0]) and torch.isnan(loss[1]) and torch.isnan(loss[2])
     _status_ok()
+
+
+@pytest.mark.parametrize("N,C,H,W,K,R,S,stride,pad", [
+    (2, 3, 17, 13, 5, 3, 3, (1, 1), (1, 1)),
+    (3, 7, 20, 9, 11, 5, 3, (2, 1), (2, 0)),
+    (1, 16, 15, 15, 130, 3, 3, (2, 2), (0, 1)),
+    (2, 65, 8, 8, 70, 1, 1, (1, 1), (0, 0)),
+])
+def test_conv2d_implicit_gemm_matches_fp32_torch(N, C, H, W, K, R, S, stride, pad):
+    """Forward, data gradient, weight and bias gradients of the implicit-GEMM
+    conv kernels against torch's conv2d in fp32 (TF32 off) at ragged shapes,
+    strides and paddings."""
+    from underhfs_b200.ops import kernels as K_
+
+    torch.backends.cudnn.allow_tf32 = False
+    gen = torch.Generator(device="cuda").manual_seed(N * 1000 + C * 10 + K)
+    x = torch.randn(N, C, H, W, device="cuda", generator=gen)
+    w = torch.randn(K, C, R, S, device="cuda", generator=gen) * 0.2
+    b = torch.randn(K, device="cuda", generator=gen)
+    y = K_.conv2d_fwd(x, w, b, stride, pad)
+    xr, wr, br = (t.clone().requires_grad_(True) for t in (x, w, b))
+    yr = torch.nn.functional.conv2d(xr, wr, br, stride, pad)
+    assert y.shape == yr.shape
+    assert torch.allclose(y, yr, rtol=1e-4, atol=1e-4), (y - yr).abs().max()
+    dy = torch.randn_like(yr)
+    yr.backward(dy)
+    dx, dw, db = K_.conv2d_bwd(dy, x, w, stride, pad, True)
+    for got, want in ((dx, xr.grad), (dw, wr.grad), (db, br.grad)):
+        err = ((got - want).abs().max() / want.abs().max()).item()
+        assert err < 1e-5, err
+    assert K_.core().device_status(True)["code"] == 0

@@ -136,7 +136,29 @@ def _case_colsum():
     return lambda: K.colsum_accum(x, out), 0, x.numel() * 2
 
 
+def _conv_inputs():
+    """3x3 conv, 64 -> 64 channels, 56 x 56, batch 32, stride 1, pad 1 (fp32)."""
+    x = torch.randn(32, 64, 56, 56, device="cuda")
+    w = torch.randn(64, 64, 3, 3, device="cuda") * 0.05
+    b = torch.randn(64, device="cuda")
+    flops = 2.0 * 32 * 64 * 56 * 56 * 64 * 9
+    return x, w, b, flops
+
+
+def _case_conv_fwd():
+    x, w, b, flops = _conv_inputs()
+    return lambda: K.conv2d_fwd(x, w, b, (1, 1), (1, 1)), flops, 2 * x.numel() * 4
+
+
+def _case_conv_bwd():
+    x, w, b, flops = _conv_inputs()
+    dy = torch.randn_like(x)
+    return lambda: K.conv2d_bwd(dy, x, w, (1, 1), (1, 1), True), 2 * flops, 3 * x.numel() * 4
+
+
 CASES: dict[str, Callable] = {
+    "conv_fwd": _case_conv_fwd,
+    "conv_bwd": _case_conv_bwd,
     "gemm_fwd": _case_gemm_fwd,
     "gemm_fwd_gelu": _case_gemm_fwd_gelu,
     "gemm_dgrad_dgelu": _case_gemm_dgrad_dgelu,

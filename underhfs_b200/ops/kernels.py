@@ -335,6 +335,9 @@ def increment_(counter: torch.Tensor) -> None:
 
 # ------------------------------------------------------------------- conv2d
 def conv2d_fwd(x, w, b, stride, padding):
+    """fp32 NCHW conv2d as an implicit GEMM (csrc/kernels/conv_igemm.cu)."""
+    x, w = x.contiguous(), w.contiguous()
+    b = b.contiguous() if b is not None else None
     N, C, H, W = x.shape
     K, _, R, S = w.shape
     sh, sw = stride
@@ -352,7 +355,7 @@ def conv2d_bwd(dy, x, w, stride, padding, need_bias):
     sh, sw = stride
     ph, pw = padding
     P, Q = dy.shape[2], dy.shape[3]
-    dy = dy.contiguous()
+    dy, x, w = dy.contiguous(), x.contiguous(), w.contiguous()
     dx = torch.empty_like(x)
     dw = torch.empty_like(w)
     db = torch.empty((K,), dtype=torch.float32, device=x.device) if need_bias else None
