@@ -461,6 +461,12 @@ def run_torch_eager(args) -> int:
 
     torch.manual_seed(0)
     model = LM().to(dev)
+    with torch.no_grad():  # GPT-style init: N(0, 0.02) weights, zero biases
+        for mod in model.modules():
+            if isinstance(mod, (tnn.Linear, tnn.Embedding)):
+                mod.weight.normal_(0.0, 0.02)
+            if isinstance(mod, tnn.Linear) and mod.bias is not None:
+                mod.bias.zero_()
     run = model
     if n > 1:
         run = tnn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,

@@ -35,6 +35,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -56,6 +57,8 @@ static_assert(2 * 128 * kSoftmaxRegs + 128 * kServiceRegs <= kThreads * kLaunchR
 constexpr float kLog2e = 1.4426950408889634f;
 // P = exp2(s - m) stays below 2^kRescaleThreshold when m is kept stale.
 constexpr float kRescaleThreshold = 8.0f;
+// default number of polynomial pairs per 8 in the forward softmax
+constexpr int kDefaultPolyPairs = 0;
 
 template <int D>
 struct FwdCfg {
@@ -105,10 +108,11 @@ struct FwdArgs {
   } while (0)
 #endif
 
-// kPolyExp: odd-indexed scores of each row use exp2_poly3 (FMA pipe) instead
-// of ex2.approx (MUFU), halving the MUFU work of the softmax (opt-in:
-// UHFS_ATTN_EXP=poly).
-template <int D, bool kPolyExp>
+// kPoly: of every 8 consecutive score pairs of a row, the first kPoly use
+// exp2_poly3_x2 (packed FMA-pipe polynomial) instead of ex2.approx (MUFU), so
+// the exponentials of a block split between the two pipes
+// (UHFS_ATTN_POLY=0|2|3|4 selects it; 0 = MUFU only).
+template <int D, int kPoly>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FwdArgs a) {
   using Cfg = FwdCfg<D>;
@@ -314,30 +318,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < BKV; ++i)
           if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
       }
+      // row max: four independent chains of three-input max (two scores each)
       float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
 #pragma unroll
-      for (int i = 4; i < BKV; i += 4) {
+      for (int i = 4; i < BKV; i += 8) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) mx4[e] = fmaxf(mx4[e], __uint_as_float(sr[i + e]));
+        for (int e = 0; e < 4; ++e)
+          mx4[e] = max3f(mx4[e], __uint_as_float(sr[i + e]), __uint_as_float(sr[i + 4 + e < BKV ? i + 4 + e : i + e]));
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
       const float m_blk = mx * a.sl2;
       const bool rescale = m_blk > m_run + kRescaleThreshold;
       const float m_new = rescale ? m_blk : m_run;
       const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.f;  // 0 while m_run = -inf
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = exp2(S * scale * log2e - m): the scale and offset as packed fp32x2
+      // FMAs, the row sum as packed adds into two accumulator pairs
+      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 sl2x2 = make_float2(a.sl2, a.sl2), nbase = make_float2(-base, -base);
       uint32_t pk[BKV / 2];
 #pragma unroll
       for (int i = 0; i < BKV / 2; ++i) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), a.sl2, -base));
-        const float x1 = fmaf(__uint_as_float(sr[2 * i + 1]), a.sl2, -base);
-        const float p1 = kPolyExp ? exp2_poly3(x1) : ex2_approx(x1);
-        rs4[(2 * i) & 3] += p0;
-        rs4[(2 * i + 1) & 3] += p1;
-        pk[i] = pack_bf16x2(p0, p1);
+        const float2 x = f2_fma(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2x2, nbase);
+        float2 pr;
+        if ((i & 7) < kPoly) {
+          pr = exp2_poly3_x2(x);
+        } else {
+          pr.x = ex2_approx(x.x);
+          pr.y = ex2_approx(x.y);
+        }
+        rs2[i & 1] = f2_add(rs2[i & 1], pr);
+        pk[i] = pack_bf16x2(pr.x, pr.y);
       }
-      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      const float2 rs = f2_add(rs2[0], rs2[1]);
+      l_run = l_run * alpha + (rs.x + rs.y);
       m_run = m_new;
       if (tracer && t == 0) FWD_TRACE(kTrExpA, j);
       // PV(j-1) finished: the P tile is free and O_t holds blocks < j
@@ -411,17 +425,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int D, bool kPolyExp>
+template <int D, int kPoly>
 void launch_fwd(const AttnParams& p, cudaStream_t s) {
   using Cfg = FwdCfg<D>;
   static PerDeviceOnce once;
   once([] {
-    UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D, kPolyExp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_tc_kernel<D, kPoly>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmem));
     // setmaxnreg redistributes exactly the launch allocation; any other
     // launch count would make the increase wait for registers that never come
     cudaFuncAttributes fa{};
-    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, kPolyExp>));
+    UHFS_CUDA_CHECK(cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, kPoly>));
     if (fa.numRegs != kLaunchRegs)
       throw std::runtime_error("fa_fwd_tc_kernel: compiled with " + std::to_string(fa.numRegs) +
                                " registers per thread, the register split needs " + std::to_string(kLaunchRegs));
@@ -441,7 +455,7 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
   a.status = device_status_ptr();
   a.trace = g_fwd_trace;
   dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
-  fa_fwd_tc_kernel<D, kPolyExp><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
+  fa_fwd_tc_kernel<D, kPoly><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -468,17 +482,24 @@ void set_attn_fwd_trace(unsigned long long* buf) {
 }
 
 void flash_attn_fwd_tc(const AttnParams& p, cudaStream_t s) {
-  static const bool poly = [] {
-    const char* e = getenv("UHFS_ATTN_EXP");
-    return e != nullptr && std::string(e) == "poly";
+  // UHFS_ATTN_POLY: score pairs (of every 8) whose exponentials use the
+  // FMA-pipe polynomial instead of MUFU
+  static const int poly = [] {
+    const char* e = getenv("UHFS_ATTN_POLY");
+    const int v = e != nullptr ? atoi(e) : kDefaultPolyPairs;
+    return (v == 0 || v == 2 || v == 3 || v == 4) ? v : kDefaultPolyPairs;
   }();
-  if (p.D == 64) {
-    if (poly) launch_fwd<64, true>(p, s);
-    else launch_fwd<64, false>(p, s);
-  } else {
-    if (poly) launch_fwd<128, true>(p, s);
-    else launch_fwd<128, false>(p, s);
-  }
+  auto go = [&](auto dtag) {
+    constexpr int D = decltype(dtag)::value;
+    switch (poly) {
+      case 2: return launch_fwd<D, 2>(p, s);
+      case 3: return launch_fwd<D, 3>(p, s);
+      case 4: return launch_fwd<D, 4>(p, s);
+      default: return launch_fwd<D, 0>(p, s);
+    }
+  };
+  if (p.D == 64) go(std::integral_constant<int, 64>{});
+  else go(std::integral_constant<int, 128>{});
 }
 
 }  // namespace uhfs

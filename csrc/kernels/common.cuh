@@ -384,6 +384,61 @@ __device__ __forceinline__ float exp2_poly3(float x) {
   return x < -125.f ? 0.f : r;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot computes both
+// halves), used by the softmax loops whose issue rate bounds them.
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "sub.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// max of three floats in one instruction (sm_100 three-input max.f32).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp2_poly3 for a pair, with the additions and the polynomial in packed
+// f32x2 instructions (the same float32 steps per half).  Inputs below -125
+// are clamped there and return 2^-125 (about 2.4e-38) instead of exactly 0,
+// which adds nothing measurable to a softmax row sum; every other input gives
+// exp2_poly3's result bit for bit.
+__device__ __forceinline__ float2 exp2_poly3_x2(float2 x) {
+  const float2 xc = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const float2 t = f2_add(xc, magic);
+  const float2 f = f2_sub(xc, f2_sub(t, magic));
+  float2 p = f2_fma(f, make_float2(0.05508868396282196f, 0.05508868396282196f),
+                    make_float2(0.24260404706001282f, 0.24260404706001282f));
+  p = f2_fma(p, f, make_float2(0.6932762265205383f, 0.6932762265205383f));
+  p = f2_fma(p, f, make_float2(0.9999289512634277f, 0.9999289512634277f));
+  // k = bits(t) - 0x4B400000 and (bits(t) << 23) == (k << 23) mod 2^32
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

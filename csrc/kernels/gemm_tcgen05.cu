@@ -210,9 +210,10 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
 
 // Epilogue operands that are read row-wise (the residual of GEMM_EPI_RESID,
 // the GELU input of GEMM_EPI_DGELU): each lane needs 64 bytes of its row per
-// 32-column chunk.  All of the warp's chunks (BN / 64 of them, 16 registers
-// each) are requested before the warp waits for the accumulator, so the
-// global-load latency overlaps that wait instead of stalling each chunk.
+// 32-column chunk.  Chunk 0 is loaded before the warp waits for the
+// accumulator and chunk j + 1 while chunk j is processed.  (Requesting every
+// chunk up front was measured slower: 116.5 against 91.9 us for the
+// 16384 x 3072 x 768 dGELU product.)
 template <int BN>
 struct AuxRegs {
   uint4 r[BN / 64][4];
@@ -277,6 +278,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
     const int c = c_begin + j;
     if (c >= c_end) break;
     const int col0 = n0 + c * 32;
+    if (j + 1 < BN / 64) epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, j + 1, aux.r[j + 1 < BN / 64 ? j + 1 : j]);
     float v[32];
     const uint32_t taddr = tmem_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32);
     tmem_ld_32x32b_x32(taddr, v);
@@ -587,8 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * BM, n0 = tn * BN;
       AuxRegs<BN> aux;
-#pragma unroll
-      for (int j = 0; j < BN / 64; ++j) epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, j, aux.r[j]);
+      epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
       if (!mbar_wait_warp(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
       tc_fence_after();
       epilogue_tile<BN, EPI, 1>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * BN), m0, n0, quarter, ehalf,
@@ -827,9 +828,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf, n0 = tn * 2 * kPairHalf;
       AuxRegs<2 * kPairHalf> aux;
-#pragma unroll
-      for (int j = 0; j < kPairHalf / 32; ++j)
-        epi_load_aux<2 * kPairHalf, EPI>(args, m0, n0, quarter, ehalf, lane, j, aux.r[j]);
+      epi_load_aux<2 * kPairHalf, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
       if (!mbar_wait_warp_cluster(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 31)) break;
       tc_fence_after();
       const uint32_t tempty_addr = tempty_leader + acc * 8;

@@ -304,7 +304,8 @@ def case_zero3_api(rank: int, world: int) -> None:
     tr = Trainer(build_model(cfg, device=dev), cfg, policy=policy_from_env(zero_stage=3))
     src = SyntheticTokens(32000, cfg.batch, cfg.seq_len, seed=3, rank=rank)
     host = torch.empty((2, cfg.batch, cfg.seq_len), dtype=torch.int64, pin_memory=True)
-    losses = [tr.step_from_host(src.next_host(host)) for _ in range(4)]
+    src.next_host(host)  # one batch per rank, stepped on repeatedly: the loss must fall
+    losses = [tr.step_from_host(host) for _ in range(4)]
     tr.release()
     assert all(l == l for l in losses) and losses[-1] < losses[0], losses
 

@@ -43,3 +43,28 @@ def test_relative_error_over_the_softmax_range():
 def test_masked_scores_give_exact_zero():
     out = _exp2_poly3(np.array([-np.inf, -1e30, -126.0, -125.5], dtype=np.float32))
     assert np.all(out == 0.0)
+
+
+def _exp2_poly3_x2(x):
+    """exp2_poly3_x2: same steps, exponent added as bits(t) << 23 and no
+    final select (inputs below -125 are clamped)."""
+    c3, c2, c1, c0 = _coefficients()
+    x = np.asarray(x, dtype=np.float32)
+    xc = np.maximum(x, np.float32(-125.0))
+    magic = np.float32(12582912.0)
+    t = (xc + magic).astype(np.float32)
+    f = (xc - (t - magic)).astype(np.float32)
+    p = (f * c3 + c2).astype(np.float32)
+    p = (p * f + c1).astype(np.float32)
+    p = (p * f + c0).astype(np.float32)
+    return (p.view(np.uint32) + (t.view(np.uint32) << np.uint32(23))).view(np.float32)
+
+
+def test_pair_variant_matches_scalar_above_the_clamp():
+    x = np.linspace(-125, 8, 200_001, dtype=np.float32)
+    assert np.array_equal(_exp2_poly3_x2(x), _exp2_poly3(x))
+
+
+def test_pair_variant_masked_scores_are_negligible():
+    out = _exp2_poly3_x2(np.array([-np.inf, -1e30, -126.0], dtype=np.float32))
+    assert np.all(out > 0) and np.all(out < 1e-37)
