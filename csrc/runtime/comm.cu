@@ -201,6 +201,110 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_kernel(const ArArgs a)
   commit_epoch(a.pp, a.rank, e);
 }
 
+// DDP all-reduce of fp32 gradients over a bf16 wire: the bucket's cast and
+// 1/world scale are fused into the transfer, so every byte that crosses
+// NVLink is bf16 (half of the fp32 two-shot's traffic).  `wire_off` is a bf16
+// staging span of the same element count in every rank's heap.  In 8-element
+// vectors (32 B of fp32, 16 B of bf16), slice r = [r*per, (r+1)*per):
+//   1. every rank casts the slices it does not own into its own wire span;
+//   2. (barrier) the owner of slice r sums its own fp32 values and every
+//      peer's bf16 wire values in fp32, scales, rounds the result to bf16,
+//      writes it (widened) into its gradients and pushes the bf16 result into
+//      every peer's wire span at the same place;
+//   3. (barrier) every rank widens the pushed results of the other slices
+//      into its gradients.
+// All ranks end with identical (bf16-rounded) gradients.  Block b handles
+// the same in-slice offsets in every phase and on every rank, so the
+// per-block cross-rank barriers order exactly the data each block touches.
+__device__ __forceinline__ uint4 pack8_bf16(const float4 x0, const float4 x1, float scale) {
+  return make_uint4(pack_bf16x2(x0.x * scale, x0.y * scale), pack_bf16x2(x0.z * scale, x0.w * scale),
+                    pack_bf16x2(x1.x * scale, x1.y * scale), pack_bf16x2(x1.z * scale, x1.w * scale));
+}
+
+__device__ __forceinline__ void unpack8_bf16(const uint4 v, float4& x0, float4& x1) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  const float2 c = __bfloat1622float2(h[2]), d = __bfloat1622float2(h[3]);
+  x0 = make_float4(a.x, a.y, b.x, b.y);
+  x1 = make_float4(c.x, c.y, d.x, d.y);
+}
+
+template <int W>
+__global__ void __launch_bounds__(kCommThreads) allreduce_wire_kernel(const ArArgs a, long long wire_off) {
+  // each vector here also carries 32 B of fp32 gradients: half the loads in
+  // flight of allreduce_kernel keeps the register count near it
+  constexpr int U = W >= 4 ? 1 : 4 / W;
+  const uint32_t e = next_epoch(a.pp, a.rank);
+  const long long nv = a.n / 8;
+  const long long per = (nv + W - 1) / W;
+  const long long G = (long long)gridDim.x * blockDim.x;
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  float4* g = reinterpret_cast<float4*>(a.pp.data[a.rank] + a.off_bytes);
+  uint4* wire = reinterpret_cast<uint4*>(a.pp.data[a.rank] + wire_off);
+  // 1. cast the slices owned by the peers
+  for (int r = 0; r < W; ++r) {
+    if (r == a.rank) continue;
+    const long long lo = per * r, hi = min(nv, lo + per);
+    for (long long i = lo + tid; i < hi; i += G) wire[i] = pack8_bf16(g[2 * i], g[2 * i + 1], 1.0f);
+  }
+  if (!block_barrier(a.pp, a.rank, W, kInOff, e, a.status, 104)) {
+    commit_epoch(a.pp, a.rank, e);
+    return;
+  }
+  // 2. reduce this rank's slice; push the rounded result to every peer
+  {
+    const long long lo = per * a.rank, hi = min(nv, lo + per);
+    for (long long base = lo + tid; base < hi; base += U * G) {
+      uint4 v[U][W];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long i = base + u * G;
+#pragma unroll
+        for (int p = 0; p < W; ++p)
+          if (p != a.rank && i < hi) v[u][p] = __ldcg(reinterpret_cast<const uint4*>(a.pp.data[p] + wire_off) + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long i = base + u * G;
+        if (i >= hi) break;
+        float4 s0 = g[2 * i], s1 = g[2 * i + 1];
+#pragma unroll
+        for (int p = 0; p < W; ++p) {
+          if (p == a.rank) continue;
+          float4 x0, x1;
+          unpack8_bf16(v[u][p], x0, x1);
+          s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
+          s1.x += x1.x; s1.y += x1.y; s1.z += x1.z; s1.w += x1.w;
+        }
+        const uint4 r = pack8_bf16(s0, s1, a.scale);
+        float4 w0, w1;
+        unpack8_bf16(r, w0, w1);
+        g[2 * i] = w0;
+        g[2 * i + 1] = w1;
+#pragma unroll
+        for (int p = 0; p < W; ++p)
+          if (p != a.rank) __stcg(reinterpret_cast<uint4*>(a.pp.data[p] + wire_off) + i, r);
+      }
+    }
+  }
+  if (!block_barrier(a.pp, a.rank, W, kOutOff, e, a.status, 105)) {
+    commit_epoch(a.pp, a.rank, e);
+    return;
+  }
+  // 3. widen the results pushed by the owners of the other slices
+  for (int r = 0; r < W; ++r) {
+    if (r == a.rank) continue;
+    const long long lo = per * r, hi = min(nv, lo + per);
+    for (long long i = lo + tid; i < hi; i += G) {
+      float4 w0, w1;
+      unpack8_bf16(__ldcg(wire + i), w0, w1);
+      g[2 * i] = w0;
+      g[2 * i + 1] = w1;
+    }
+  }
+  commit_epoch(a.pp, a.rank, e);
+}
+
 // NVLS all-reduce (NVSwitch in-switch reduction), fp32, in place.  `mc` is
 // the multicast address of a buffer whose every rank's copy is bound to one
 // NVLink multicast object; the cross-rank barriers use this heap's signal
@@ -680,6 +784,26 @@ void comm_allreduce_f32_nvls(const SymmetricHeap& h, uintptr_t mc_base, long lon
 void comm_allreduce_bf16(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
                          cudaStream_t s) {
   launch_allreduce(h, off_bytes, n, scale, blocks, true, s);
+}
+
+void comm_allreduce_f32_wire_bf16(const SymmetricHeap& h, long long off_bytes, long long wire_off_bytes, long long n,
+                                  float scale, int blocks, cudaStream_t s) {
+  if (n % 8 != 0 || off_bytes % 16 != 0 || wire_off_bytes % 16 != 0)
+    throw std::invalid_argument("bf16-wire allreduce needs 16-byte aligned spans of whole 8-element vectors");
+  if (n <= 0) return;
+  if (wire_off_bytes + 2 * n > (long long)h.data_bytes() || off_bytes + 4 * n > (long long)h.data_bytes())
+    throw std::invalid_argument("bf16-wire allreduce span outside the symmetric heap");
+  ArArgs a{};
+  a.pp = peer_ptrs(h);
+  a.off_bytes = off_bytes;
+  a.n = n;
+  a.scale = scale;
+  a.rank = h.rank();
+  a.world = h.world();
+  a.status = device_status_ptr();
+  UHFS_WORLD_DISPATCH(a.world, (allreduce_wire_kernel<W><<<clamp_blocks(blocks), kCommThreads, 0, s>>>(a, wire_off_bytes)))
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
 }
 
 void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long long out_off_bytes, long long n,

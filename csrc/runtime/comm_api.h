@@ -54,6 +54,11 @@ void comm_rs_adamw_ag(const SymmetricHeap& grads, long long g_off_bytes, const S
 void comm_allgather(const SymmetricHeap& h, long long off_bytes, long long shard_bytes, int blocks, cudaStream_t s);
 void comm_allreduce_bf16(const SymmetricHeap& h, long long off_bytes, long long n, float scale, int blocks,
                          cudaStream_t s);
+// In-place fp32 all-reduce whose transfers are bf16 (cast and scale fused);
+// `wire_off_bytes` is a bf16 staging span of n elements in every rank's heap.
+// Every rank ends with the same bf16-rounded sum (widened to fp32).
+void comm_allreduce_f32_wire_bf16(const SymmetricHeap& h, long long off_bytes, long long wire_off_bytes, long long n,
+                                  float scale, int blocks, cudaStream_t s);
 void comm_reduce_scatter(const SymmetricHeap& h, long long in_off_bytes, long long out_off_bytes, long long n,
                          bool bf16, float scale, int blocks, cudaStream_t s);
 void comm_gather_segments(const SymmetricHeap& h, long long dst_off_bytes, uintptr_t shard,

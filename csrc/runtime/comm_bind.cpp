@@ -116,6 +116,10 @@ void bind_comm(py::module_& m) {
   });
   m.def("comm_allreduce_bf16", [](const SymmetricHeap& h, long long off, long long n, float scale, int blocks,
                                   uintptr_t s) { comm_allreduce_bf16(h, off, n, scale, blocks, S(s)); });
+  m.def("comm_allreduce_f32_wire_bf16", [](const SymmetricHeap& h, long long off, long long wire_off, long long n,
+                                           float scale, int blocks, uintptr_t s) {
+    comm_allreduce_f32_wire_bf16(h, off, wire_off, n, scale, blocks, S(s));
+  });
   m.def("comm_reduce_scatter", [](const SymmetricHeap& h, long long in_off, long long out_off, long long n, bool bf16,
                                   float scale, int blocks, uintptr_t s) {
     comm_reduce_scatter(h, in_off, out_off, n, bf16, scale, blocks, S(s));

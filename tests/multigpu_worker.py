@@ -120,6 +120,43 @@ def case_ddp(rank: int, world: int) -> None:
     assert core().device_status(True)["code"] == 0
 
 
+def case_ddp_wire(rank: int, world: int) -> None:
+    """DDP with bf16 transport (UNDERHFS_DDP_WIRE=bf16): the averaged gradients
+    match NCCL's fp32 all-reduce to bf16 rounding and are identical on every
+    rank (replicas stay in step)."""
+    os.environ["UNDERHFS_DDP_WIRE"] = "bf16"
+    from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
+
+    gen = torch.Generator().manual_seed(700 + rank)
+    ids = torch.randint(0, 1024, (2, 256), generator=gen).cuda()
+    tg = torch.roll(ids, -1, 1)
+    ref_model = _model()
+    ref_model.zero_grad()
+    ref_model(ids, tg).backward()
+    ref = ref_model.flat.grads.clone()
+    dist.all_reduce(ref)
+    ref /= world
+    model = _model()
+    ddp = DistributedDataParallel(model, policy_from_env(), bucket_mb=0.25)
+    assert ddp._bucketer.wire
+    for _ in range(2):
+        model.zero_grad()
+        ddp(ids, tg).backward()
+        ddp.synchronize_gradients()
+        torch.cuda.synchronize()
+        g = model.flat.grads[: ref.numel()]
+        # each contribution and the result are rounded to bf16 (2^-9 relative)
+        assert ((g - ref).norm() / ref.norm()).item() < 1e-2
+        assert ((g - ref).abs().max() / ref.abs().max()).item() < 2e-2
+        gathered = [torch.empty_like(g) for _ in range(world)]
+        dist.all_gather(gathered, g)
+        assert all(torch.equal(gathered[0], x) for x in gathered[1:]), "ranks disagree"
+    from underhfs_b200.ops._lib import core
+
+    assert core().device_status(True)["code"] == 0
+    del os.environ["UNDERHFS_DDP_WIRE"]
+
+
 def case_nvls(rank: int, world: int) -> None:
     """DDP gradients reduced in the NVSwitch (multimem) match NCCL's.
 
@@ -379,7 +416,7 @@ def main() -> int:
     case = sys.argv[1]
     rank, world = _setup()
     try:
-        cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3, "zero3_api": case_zero3_api,
+        cases = {"allreduce": case_allreduce, "ddp": case_ddp, "zero": case_zero, "zero3": case_zero3, "zero3_api": case_zero3_api, "ddp_wire": case_ddp_wire,
                  "native": case_native, "cp": case_cp, "nvls": case_nvls}
         cases[case](rank, world)
         dist.barrier()

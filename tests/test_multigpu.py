@@ -32,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["allreduce", "ddp", "zero", "zero3", "zero3_api", "native", "cp", "nvls"])
+@pytest.mark.parametrize("case", ["allreduce", "ddp", "ddp_wire", "zero", "zero3", "zero3_api", "native", "cp", "nvls"])
 def test_two_gpu_case(case):
     if _gpus() < 2:
         pytest.skip("needs two GPUs")

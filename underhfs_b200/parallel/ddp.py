@@ -37,7 +37,11 @@ class BucketedAllReduce:
         self.blocks = blocks
         self.use_nccl = use_nccl
         flat = model.flat
-        n = (flat.numel + 3) // 4 * 4
+        # UNDERHFS_DDP_WIRE=bf16: gradients cross NVLink as bf16 (cast and
+        # scale fused into the all-reduce kernel, fp32 accumulation; every rank
+        # ends with the same bf16-rounded gradient), half the bytes of fp32
+        self.wire = os.environ.get("UNDERHFS_DDP_WIRE", "fp32") == "bf16" and not use_nccl
+        n = (flat.numel + 7) // 8 * 8
         # UNDERHFS_NVLS=1: gradients in memory bound to an NVLink multicast
         # object (allocated through torch's symmetric memory), reduced in the
         # switch by allreduce_nvls_f32_kernel; this heap then only carries the
@@ -45,13 +49,18 @@ class BucketedAllReduce:
         # system offers no multicast.
         self.mc = 0
         grads = self._nvls_grads(n) if os.environ.get("UNDERHFS_NVLS", "0") == "1" and not use_nccl else None
-        self.sym = SymmetricBuffer(4096 if grads is not None else n * 4, rank=self.rank, world=self.world)
+        if grads is not None:
+            self.wire = False
+        nbytes = 4096 if grads is not None else n * 4 + (n * 2 + 256 if self.wire else 0)
+        self.sym = SymmetricBuffer(nbytes, rank=self.rank, world=self.world)
         if grads is None:
             grads = self.sym.tensor(n, torch.float32)
+        self.wire_off = self.sym.tensor(n, torch.bfloat16).data_ptr() - self.sym.heap.data_ptr(self.rank) \
+            if self.wire else 0
         model.rehome_buffers(grads=grads)
         self.flat = model.flat
         self.n = n
-        per = max(4, (bucket_bytes // 4) // 4 * 4)
+        per = max(8, (bucket_bytes // 4) // 8 * 8)
         edges = list(range(n, 0, -per)) + [0]
         self.buckets = [(edges[i + 1], edges[i]) for i in range(len(edges) - 1)]  # descending ranges
         self.stream = torch.cuda.Stream(priority=-1)
@@ -120,6 +129,9 @@ class BucketedAllReduce:
                 dist.all_reduce(view)
                 if self.scale != 1.0:
                     view.mul_(self.scale)
+            elif self.wire:
+                core().comm_allreduce_f32_wire_bf16(self.sym.heap, lo * 4, self.wire_off + lo * 2, hi - lo,
+                                                    self.scale, self.blocks, self.stream.cuda_stream)
             elif self.mc:
                 core().comm_allreduce_f32_nvls(self.sym.heap, self.mc, lo * 4, hi - lo, self.scale, self.blocks,
                                                self.stream.cuda_stream)
