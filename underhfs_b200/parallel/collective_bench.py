@@ -66,8 +66,14 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--min-kib", type=int, default=1)
     ap.add_argument("--max-mib", type=int, default=1024)
     ap.add_argument("--step", type=int, default=4, help="size multiplier between points (2 = every power of two)")
-    ap.add_argument("--ops", default="allreduce,reduce_scatter,allgather")
+    ap.add_argument("--ops", default="allreduce,reduce_scatter,allgather",
+                    help="comma list of allreduce, allreduce_wire (fp32 over a bf16 wire), reduce_scatter, allgather")
+    ap.add_argument("--fused-params", default="",
+                    help="comma list of parameter counts (e.g. 125e6,1.3e9): time the fused ZeRO-2 step "
+                         "(reduce-scatter + AdamW + all-gather) and report it against its roofline")
     args = ap.parse_args(argv)
+    if args.fused_params:
+        return fused_step_bench([int(float(v)) for v in args.fused_params.split(",")])
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
@@ -99,7 +105,22 @@ def main(argv: list[str] | None = None) -> int:
                 buf = sym.tensor(n, dtype, offset_bytes=off_in)
                 out = sym.tensor(n, dtype, offset_bytes=off_out)
                 for op in args.ops.split(","):
-                    if op == "allreduce":
+                    if op == "allreduce_wire" and bf16:
+                        continue  # the wire variant reduces fp32 gradients
+                    if op == "allreduce_wire":
+                        # fp32 gradients over a bf16 wire; the staging span follows the data
+                        ref = x.clone()
+                        dist.all_reduce(ref)
+                        buf.copy_(x)
+                        c.comm_allreduce_f32_wire_bf16(sym.heap, off_in, off_out, n, 1.0, blocks, stream)
+                        torch.cuda.synchronize()
+                        err = (buf.float() - ref.float()).abs().max().item() / max(1.0, ref.float().abs().max().item())
+                        t_ours = _time(lambda: c.comm_allreduce_f32_wire_bf16(sym.heap, off_in, off_out, n,
+                                                                              1.0 / world, blocks, stream), iters)
+                        nccl_t = x.clone()
+                        t_nccl = _time(lambda: dist.all_reduce(nccl_t, op=dist.ReduceOp.AVG), iters)
+                        factor = 2.0 * (world - 1) / world  # bus bytes counted at fp32 width
+                    elif op == "allreduce":
                         ref = x.clone()
                         dist.all_reduce(ref)
                         buf.copy_(x)
@@ -143,7 +164,7 @@ def main(argv: list[str] | None = None) -> int:
                         factor = (world - 1) / world
                     st = c.device_status(True)
                     assert st["code"] == 0, st
-                    tol = 2e-2 if bf16 else 1e-5
+                    tol = 2e-2 if (bf16 or op == "allreduce_wire") else 1e-5
                     assert err <= tol, (op, dtype, nbytes, err)
                     for impl, t in (("ours", t_ours), ("nccl", t_nccl)):
                         bus = nbytes * factor / (t * 1e-3) / 1e9
@@ -166,6 +187,65 @@ def main(argv: list[str] | None = None) -> int:
         torch.cuda.synchronize()
         dist.barrier()
         sym.close()
+        dist.destroy_process_group()
+    return 0
+
+
+PEER_GBS = 770.0   # measured peer copy per direction per GPU on this class of node
+HBM_GBS = 6537.0   # measured device copy bandwidth (read + write)
+
+
+def fused_step_bench(param_counts: list[int]) -> int:
+    """The ZeRO-2 step kernel (rs_adamw_ag_kernel) on n fp32 gradients / bf16
+    parameters in symmetric memory.  Per GPU and direction it moves
+    (W-1)/W x 6n bytes over NVLink (fp32 shard reads + bf16 parameter pushes
+    each way) and about 6n + 24n/W bytes of HBM (gradients and parameters, plus
+    fp32 master / moments of the owned shard read and written); the roofline
+    time is the larger of the two at the measured rates, and the line reports
+    achieved / roofline."""
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    c = core()
+    stream = torch.cuda.current_stream().cuda_stream
+    try:
+        for n in param_counts:
+            unit = 8 * world
+            n = (n + unit - 1) // unit * unit
+            shard = n // world
+            gsym = SymmetricBuffer(n * 4 + 4096, rank=rank, world=world)
+            psym = SymmetricBuffer(n * 2 + 4096, rank=rank, world=world)
+            grads = gsym.tensor(n, torch.float32, offset_bytes=0)
+            params = psym.tensor(n, torch.bfloat16, offset_bytes=0)
+            grads.normal_()
+            params.zero_()
+            master = torch.randn(shard, device="cuda") * 0.02
+            m = torch.zeros(shard, device="cuda")
+            v = torch.zeros(shard, device="cuda")
+            step = torch.zeros((), dtype=torch.int32, device="cuda")
+            blocks = 132
+
+            def run():
+                c.comm_rs_adamw_ag(gsym.heap, 0, psym.heap, 0, rank * shard, shard, master.data_ptr(), m.data_ptr(),
+                                   v.data_ptr(), 1e-4, 0.9, 0.95, 1e-8, 0.1, 1.0 / world, True, step.data_ptr(),
+                                   blocks, stream)
+
+            ms = _time(run, 10)
+            st = c.device_status(True)
+            assert st["code"] == 0, st
+            link_s = (world - 1) / world * 6.0 * n / (PEER_GBS * 1e9)
+            hbm_s = (6.0 * n + 24.0 * n / world) / (HBM_GBS * 1e9)
+            bound_ms = 1e3 * max(link_s, hbm_s)
+            if rank == 0:
+                print(json.dumps({"op": "zero2_rs_adamw_ag", "params": n, "n_gpus": world, "ms": ms,
+                                  "roofline_ms": bound_ms, "bound": "nvlink" if link_s >= hbm_s else "hbm",
+                                  "frac_of_roofline": bound_ms / ms}), flush=True)
+            gsym.close()
+            psym.close()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
         dist.destroy_process_group()
     return 0
 
