@@ -299,7 +299,8 @@ def run_ours(args) -> int:
                                      if cc["zero"] == 0 else
                                      f"ZeRO-2 AdamW lr 3e-4, betas (0.9, 0.95), weight decay {cfg.weight_decay} "
                                      "(decoupled): fused NVLink reduce-scatter + AdamW + all-gather kernel"),
-                       "grad_allreduce": ("fused NVLink two-shot kernel, 25 MB buckets overlapped with backward"
+                       "grad_allreduce": ((f"fused NVLink two-shot kernel ({os.environ.get('UNDERHFS_DDP_WIRE', 'fp32')} "
+                                           "on the wire), 25 MB buckets overlapped with backward")
                                           if cc["zero"] == 0 else "reduce-scatter fused with the AdamW update"),
                        "cuda_graph": not args.no_graph,
                        "l2": "no flush: per-step working set (weights, grads, moments, activations) >> 126 MB L2"},

@@ -84,12 +84,15 @@ def case_ddp(rank: int, world: int) -> None:
         assert err < 1e-4, err
     # optimizer step split around the last (embedding) all-reduce: the same
     # weights as one step after every reduction.  The weight-gradient GEMMs
-    # accumulate with fp32 atomics, so two runs differ in the last bits; eps
-    # 1e-3 keeps Adam from turning those into sign flips of near-zero updates.
+    # and the dQ accumulation add with fp32 atomics in a varying order, and a
+    # last-bit change of an fp32 sum can flip a bf16 activation by one ulp, so
+    # two identical runs differ slightly: the split run is compared with the
+    # spread of two unsplit runs.  eps 1e-3 keeps Adam from turning that noise
+    # into sign flips of near-zero updates.
     from underhfs_b200.optim import FusedAdamW
 
     outs = []
-    for split in (False, True):
+    for split in (False, False, True):
         m2 = _model()
         d2 = DistributedDataParallel(m2, policy_from_env(), bucket_mb=0.25)
         opt = FusedAdamW(m2.parameters(), lr=1e-3, betas=(0.9, 0.95), eps=1e-3, weight_decay=0.1, decoupled=True)
@@ -106,8 +109,11 @@ def case_ddp(rank: int, world: int) -> None:
         torch.cuda.synchronize()
         outs.append(m2.flat.master.clone())
     moved = (outs[0] - _model().flat.master).abs().max().item()  # how far two steps moved the weights
-    diff = (outs[0] - outs[1]).abs().max().item()
-    assert diff < 1e-3 * moved, (diff, moved)
+    spread = (outs[0] - outs[1]).abs().max().item()  # two unsplit runs
+    diff = max((outs[2] - o).abs().max().item() for o in outs[:2])
+    if rank == 0:
+        print(f"split step: moved {moved:.3e}, unsplit spread {spread:.3e}, split diff {diff:.3e}", flush=True)
+    assert diff <= 4.0 * spread + 1e-4 * moved, (diff, spread, moved)
     with ddp.no_sync():
         model.zero_grad()
         ddp(ids, tg).backward()

@@ -54,6 +54,14 @@ def _case_gemm_wgrad():
     return lambda: K.linear_wgrad_accum(dy, x, dw), 2.0 * TOKENS * 2304 * 768, 0
 
 
+def _wgrad_case(n_out: int, n_in: int):
+    def case():
+        dy, x = _bf(TOKENS, n_out), _bf(TOKENS, n_in)
+        dw = torch.zeros(n_out, n_in, device="cuda")
+        return lambda: K.linear_wgrad_accum(dy, x, dw), 2.0 * TOKENS * n_out * n_in, 0
+    return case
+
+
 def _case_gemm_8192():
     a, b = _bf(8192, 8192, scale=0.02), _bf(8192, 8192, scale=0.02)
     return lambda: K.linear_fwd(a, b), 2.0 * 8192 ** 3, 0
@@ -164,6 +172,11 @@ CASES: dict[str, Callable] = {
     "gemm_dgrad_dgelu": _case_gemm_dgrad_dgelu,
     "gemm_wgrad": _case_gemm_wgrad,
     "gemm_8192": _case_gemm_8192,
+    # every weight gradient of the 125M step (16384 tokens): fc1, fc2, out-proj, tied head
+    "wgrad_fc1": _wgrad_case(3072, 768),
+    "wgrad_fc2": _wgrad_case(768, 3072),
+    "wgrad_o": _wgrad_case(768, 768),
+    "wgrad_head": _wgrad_case(32000, 768),
     "attn_fwd": _case_attn_fwd,
     "attn_bwd": _case_attn_bwd,
     "rmsnorm_fwd": _case_rmsnorm_fwd,

@@ -9,6 +9,7 @@ its docstring on the current stream.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -133,6 +134,11 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, gelu_in: torch.Tensor | None
     return dx
 
 
+# UHFS_WGRAD_SPLITS=<n>: weight gradients as classic split-K with n splits
+# (split-major unit order) instead of stream-K, for comparisons
+_WGRAD_SPLITS = int(os.environ.get("UHFS_WGRAD_SPLITS", "0") or 0)
+
+
 def linear_wgrad_accum(dy: torch.Tensor, x: torch.Tensor, dw32: torch.Tensor, splits: int = 0) -> None:
     """dw32[N,K] += dy[M,N]^T x[M,K]  (fp32, atomic accumulation).
 
@@ -142,6 +148,8 @@ def linear_wgrad_accum(dy: torch.Tensor, x: torch.Tensor, dw32: torch.Tensor, sp
     """
     M, N = dy.shape
     K = x.shape[1]
+    if splits == 0 and _WGRAD_SPLITS:
+        splits = _WGRAD_SPLITS
     if splits == 0 and math.ceil(N / 128) * math.ceil(K / 256) >= 4 * NUM_SMS:
         splits = 1  # enough tiles for >= 4 full waves: plain tiles keep better L2 reuse
     gemm_raw(N, K, M, dy, dy.stride(0), True, x, x.stride(0), True, dw32, dw32.stride(0), EPI_F32_ACCUM,

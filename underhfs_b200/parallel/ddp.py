@@ -35,6 +35,7 @@ class BucketedAllReduce:
         self.rank = policy.rank
         self.scale = 1.0 / self.world if average else 1.0
         self.blocks = blocks
+        self.tail_blocks = int(os.environ.get("UNDERHFS_DDP_TAIL_BLOCKS", "148"))
         self.use_nccl = use_nccl
         flat = model.flat
         # UNDERHFS_DDP_WIRE=bf16: gradients cross NVLink as bf16 (cast and
@@ -105,7 +106,8 @@ class BucketedAllReduce:
         self._launched_any = False
         self.model.engine.grad_ready = self.on_ready if enabled else None
 
-    def _launch(self, lo: int, hi: int) -> None:
+    def _launch(self, lo: int, hi: int, blocks: int | None = None) -> None:
+        blocks = self.blocks if blocks is None else blocks
         nvtx.push(f"allreduce/bucket[{lo},{hi})")
         compute = torch.cuda.current_stream()
         # every reduction launched before this one is done at `pre`
@@ -131,12 +133,12 @@ class BucketedAllReduce:
                     view.mul_(self.scale)
             elif self.wire:
                 core().comm_allreduce_f32_wire_bf16(self.sym.heap, lo * 4, self.wire_off + lo * 2, hi - lo,
-                                                    self.scale, self.blocks, self.stream.cuda_stream)
+                                                    self.scale, blocks, self.stream.cuda_stream)
             elif self.mc:
-                core().comm_allreduce_f32_nvls(self.sym.heap, self.mc, lo * 4, hi - lo, self.scale, self.blocks,
+                core().comm_allreduce_f32_nvls(self.sym.heap, self.mc, lo * 4, hi - lo, self.scale, blocks,
                                                self.stream.cuda_stream)
             else:
-                core().comm_allreduce_f32(self.sym.heap, lo * 4, hi - lo, self.scale, self.blocks,
+                core().comm_allreduce_f32(self.sym.heap, lo * 4, hi - lo, self.scale, blocks,
                                           self.stream.cuda_stream)
             if self.trace:
                 s1 = torch.cuda.Event(enable_timing=True)
@@ -164,7 +166,9 @@ class BucketedAllReduce:
         # the rest (the embeddings, final only after the last kernel of the
         # backward) in one launch: no per-bucket synchronisation in the tail
         if self._next < len(self.buckets):
-            self._launch(self.buckets[-1][0], self.buckets[self._next][1])
+            # nothing else runs once the backward is done: the tail reduction
+            # gets enough CTAs to keep every SM's peer loads in flight
+            self._launch(self.buckets[-1][0], self.buckets[self._next][1], blocks=self.tail_blocks)
             self._next = len(self.buckets)
         if self.trace:
             end = torch.cuda.Event(enable_timing=True)
