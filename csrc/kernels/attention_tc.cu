@@ -60,16 +60,27 @@ constexpr float kRescaleThreshold = 8.0f;
 // default number of polynomial pairs per 8 in the forward softmax
 constexpr int kDefaultPolyPairs = 0;
 
+// P placement.  D = 64: P (bf16 pairs, 64 columns per tile) lives in TMEM
+// next to S and O, and PV reads it there (tcgen05.mma with A from TMEM), so
+// the only shared-memory operands are Q, K and V -- an S product of M=N=128,
+// K=16 reads 8 KB of operands per 68 tensor cycles, close to the 128 B/clk
+// of shared memory, which made the shared-memory P tile (written by the
+// softmax, read by PV) the limit of the loop.  D = 128: TMEM is full with S
+// and O, P stays a 128B-swizzled shared tile.
 template <int D>
 struct FwdCfg {
+  static constexpr bool kPTmem = (D == 64);
   static constexpr int kTile = 128 * D * 2;            // one 128 x D bf16 tile (D/64 swizzled sub-tiles)
-  static constexpr int kSlots = (D == 64) ? 4 : 3;      // K / V ring
+  static constexpr int kSlots = (D == 64) ? 6 : 3;      // K / V ring
   static constexpr int kPBytes = BQ * BKV * 2;          // P tile (2 sub-tiles of 128 x 64)
   static constexpr int kBars = 1 + 2 * kSlots + 2 * 4 + 1;
-  static constexpr int kSmem = 1024 + 2 * kTile + kSlots * kTile + 2 * kPBytes + kBars * 8 + 16;
+  static constexpr int kSmem = 1024 + 2 * kTile + kSlots * kTile + (kPTmem ? 0 : 2 * kPBytes) + kBars * 8 + 16;
   static constexpr uint32_t kSCol = 0;                  // S_A [0,128), S_B [128,256)
   static constexpr uint32_t kOCol = 2 * BKV;            // O_A, O_B: D columns each
+  static constexpr uint32_t kPCol = 2 * BKV + 2 * D;    // D = 64: P_A, P_B: 64 columns each
   static constexpr uint32_t kTmemCols = 512;
+  static_assert(!kPTmem || kPCol + 2 * (BKV / 2) <= kTmemCols, "P columns");
+  static_assert(kSmem <= 227 * 1024, "attention forward shared memory");
 };
 
 // Optional per-block clock stamps (clock64) for the CTAs of head 0 of batch 0:
@@ -123,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;                               // [2 tiles]
   uint8_t* sRing = sQ + 2 * Cfg::kTile;             // [NS slots]
   uint8_t* sP = sRing + NS * Cfg::kTile;            // [2 tiles]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (Cfg::kPTmem ? 0 : 2 * Cfg::kPBytes));
   uint64_t* q_full = bars;
   uint64_t* slot_full = bars + 1;
   uint64_t* slot_empty = slot_full + NS;
@@ -240,9 +251,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t bd = mnmaj + ring16 + slot_of(2 * j + 1) * (Cfg::kTile >> 4);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t aoff = ((kk >> 2) * (BQ * 128) + (kk & 3) * 32) >> 4;
-          tc_mma_f16(tmem + Cfg::kOCol + t * D, ad + aoff, bd + ((kk * 16 * 128) >> 4), idesc_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (Cfg::kPTmem) {
+            // A = P_t from TMEM: keys [16 kk, 16 kk + 16) are columns [8 kk, 8 kk + 8)
+            tc_mma_f16_ts(tmem + Cfg::kOCol + t * D, tmem + Cfg::kPCol + t * (BKV / 2) + (uint32_t)(kk * 8),
+                          bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
+          } else {
+            const uint32_t aoff = ((kk >> 2) * (BQ * 128) + (kk & 3) * 32) >> 4;
+            tc_mma_f16(tmem + Cfg::kOCol + t * D, ad + aoff, bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
+          }
         }
         tc_commit(&o_done[t]);
         return true;
@@ -293,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_col = lane_base + Cfg::kSCol + t * BKV;
     const uint32_t o_col = lane_base + Cfg::kOCol + t * D;
     uint8_t* prow = sP + t * Cfg::kPBytes + r * 128;
+    const uint32_t p_col = lane_base + Cfg::kPCol + t * (BKV / 2);
     const int key_limit = a.causal ? min(q + 1, T) : T;  // keys [0, key_limit) are visible
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -375,15 +393,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
-      // P row -> swizzled A tile: 16 chunks of 8 keys, chunk ch of sub-tile ch / 8
+      if constexpr (Cfg::kPTmem) {
+        // P row -> TMEM lane r: column c holds keys 2c, 2c + 1
+        tmem_st_32x32b_x32(p_col, pk);
+        tmem_st_32x32b_x32(p_col + 32, pk + 32);
+        tmem_wait_st();
+      } else {
+        // P row -> swizzled A tile: 16 chunks of 8 keys, chunk ch of sub-tile ch / 8
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int sub = ch >> 3, c8 = ch & 7;
-        const uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(prow + sub * (BQ * 128) + ((c8 ^ (r & 7)) << 4)) = v;
+        for (int ch = 0; ch < 16; ++ch) {
+          const int sub = ch >> 3, c8 = ch & 7;
+          const uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+          *reinterpret_cast<uint4*>(prow + sub * (BQ * 128) + ((c8 ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();  // P stores visible to the tensor core
       }
-      fence_proxy_async_smem();  // P stores visible to the tensor core
-      tc_fence_before();         // O rescale stores ordered before the next MMA
+      tc_fence_before();  // P / O rescale TMEM stores ordered before the next MMA
       mbar_arrive(&p_full[t]);
       if (tracer) FWD_TRACE(t == 0 ? kTrPFullA : kTrPFullB, j);
     }

@@ -78,6 +78,18 @@ def _case_attn_fwd():
     return lambda: K.flash_attn_qkv(qkv, B, T, H, D, True), 2.0 * B * H * T * T * D, 0
 
 
+def _case_attn_fwd16():
+    """The forward at the 125M step's shape: B=16 T=1024 H=12 D=64, causal."""
+    qkv, _, _, (B, T, H, D) = _attn_inputs(B=16)
+    return lambda: K.flash_attn_qkv(qkv, B, T, H, D, True), 2.0 * B * H * T * T * D, 0
+
+
+def _case_attn_bwd16():
+    qkv, o, lse, (B, T, H, D) = _attn_inputs(B=16)
+    do = _bf(B * T, H * D)
+    return (lambda: K.flash_attn_qkv_backward(qkv, o, lse, do, B, T, H, D, True), 5.0 * B * H * T * T * D, 0)
+
+
 def _case_attn_bwd():
     qkv, o, lse, (B, T, H, D) = _attn_inputs()
     do = _bf(B * T, H * D)
@@ -178,6 +190,8 @@ CASES: dict[str, Callable] = {
     "wgrad_o": _wgrad_case(768, 768),
     "wgrad_head": _wgrad_case(32000, 768),
     "attn_fwd": _case_attn_fwd,
+    "attn_fwd16": _case_attn_fwd16,
+    "attn_bwd16": _case_attn_bwd16,
     "attn_bwd": _case_attn_bwd,
     "rmsnorm_fwd": _case_rmsnorm_fwd,
     "rmsnorm_bwd": _case_rmsnorm_bwd,
