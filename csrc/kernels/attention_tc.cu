@@ -33,6 +33,7 @@
 // Python attention of nn.py:229-271.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <type_traits>
@@ -103,6 +104,7 @@ struct FwdArgs {
   float* lse;             // [B, H, T] (log2 domain)
   DeviceStatus* status;
   unsigned long long* trace;
+  int trace_bh;  // (batch, head) whose CTAs are traced (UHFS_ATTN_TRACE_BH, trace builds)
 };
 
 // Compiled in only with -DUHFS_ATTN_TRACE (UNDERHFS_ATTN_TRACE=1 at build
@@ -110,7 +112,7 @@ struct FwdArgs {
 #ifdef UHFS_ATTN_TRACE
 #define FWD_TRACE(ev, step)                                                                              \
   do {                                                                                                   \
-    if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
+    if (a.trace != nullptr && (int)blockIdx.y == a.trace_bh && (step) < kTraceSteps)                       \
       a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
 #else
@@ -479,6 +481,12 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
   a.lse = p.lse;
   a.status = device_status_ptr();
   a.trace = g_fwd_trace;
+#ifdef UHFS_ATTN_TRACE
+  {
+    const char* e = getenv("UHFS_ATTN_TRACE_BH");
+    a.trace_bh = e != nullptr ? atoi(e) : 0;
+  }
+#endif
   dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
   fa_fwd_tc_kernel<D, kPoly><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();

@@ -46,6 +46,7 @@
 // Every wait is bounded.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -114,6 +115,7 @@ struct BwdArgs {
   __nv_bfloat16* dqkv;  // [B*T, 3F]
   DeviceStatus* status;
   unsigned long long* trace;
+  int trace_bh;  // (batch, head) whose CTAs are traced (UHFS_ATTN_TRACE_BH, trace builds)
 };
 
 // Compiled in only with -DUHFS_ATTN_TRACE (UNDERHFS_ATTN_TRACE=1 at build
@@ -121,7 +123,7 @@ struct BwdArgs {
 #ifdef UHFS_ATTN_TRACE
 #define BWD_TRACE(ev, step)                                                                              \
   do {                                                                                                   \
-    if (a.trace != nullptr && blockIdx.y == 0 && (step) < kTraceSteps)                                   \
+    if (a.trace != nullptr && (int)blockIdx.y == a.trace_bh && (step) < kTraceSteps)                       \
       a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
 #else
@@ -587,6 +589,12 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
   a.dqkv = p.dq;
   a.status = device_status_ptr();
   a.trace = g_bwd_trace;
+#ifdef UHFS_ATTN_TRACE
+  {
+    const char* e = getenv("UHFS_ATTN_TRACE_BH");
+    a.trace_bh = e != nullptr ? atoi(e) : 0;
+  }
+#endif
   dim3 grid((p.f.T + BK - 1) / BK, p.f.B * p.f.H);
   fa_bwd_tc_kernel<D><<<grid, kThreads, Cfg::kSmem, s>>>(tq, td, tdq, a);
   note_launch();
