@@ -53,7 +53,7 @@ constexpr int BKV = 128;  // keys per block
 constexpr int kThreads = 384;       // 3 warpgroups
 constexpr int kLaunchRegs = 168;    // 65536 / 384, rounded down to 8
 constexpr int kSoftmaxRegs = 200;
-constexpr int kServiceRegs = 96;    // 2 * 128 * 200 + 128 * 96 <= 384 * 168
+constexpr int kServiceRegs = 104;   // 2 * 128 * 200 + 128 * 104 == 384 * 168
 static_assert(2 * 128 * kSoftmaxRegs + 128 * kServiceRegs <= kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 // P = exp2(s - m) stays below 2^kRescaleThreshold when m is kept stale.
@@ -74,7 +74,7 @@ struct FwdCfg {
   static constexpr int kTile = 128 * D * 2;            // one 128 x D bf16 tile (D/64 swizzled sub-tiles)
   static constexpr int kSlots = (D == 64) ? 6 : 3;      // K / V ring
   static constexpr int kPBytes = BQ * BKV * 2;          // P tile (2 sub-tiles of 128 x 64)
-  static constexpr int kBars = 1 + 2 * kSlots + 2 * 4 + 1;
+  static constexpr int kBars = 2 + 2 * kSlots + 2 * 5 + 1;
   static constexpr int kSmem = 1024 + 2 * kTile + kSlots * kTile + (kPTmem ? 0 : 2 * kPBytes) + kBars * 8 + 16;
   static constexpr uint32_t kSCol = 0;                  // S_A [0,128), S_B [128,256)
   static constexpr uint32_t kOCol = 2 * BKV;            // O_A, O_B: D columns each
@@ -95,7 +95,7 @@ enum FwdTraceEvent {
 unsigned long long* g_fwd_trace = nullptr;
 
 struct FwdArgs {
-  int H, T;
+  int H, T, BH;           // heads, sequence length, batch * heads
   long long F;            // H * D (columns per q / k / v section)
   float sl2;              // softmax scale * log2(e)
   int causal;
@@ -110,14 +110,14 @@ struct FwdArgs {
 // Compiled in only with -DUHFS_ATTN_TRACE (UNDERHFS_ATTN_TRACE=1 at build
 // time); the product build has no stamps and no trace pointer test.
 #ifdef UHFS_ATTN_TRACE
-#define FWD_TRACE(ev, step)                                                                              \
+#define FWD_TRACE(cta, ev, step)                                                                         \
   do {                                                                                                   \
-    if (a.trace != nullptr && (int)blockIdx.y == a.trace_bh && (step) < kTraceSteps)                       \
-      a.trace[((long long)blockIdx.x * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
+    if (tr_on && (step) < kTraceSteps)                                                                   \
+      a.trace[((long long)(cta) * kTraceEvents + (ev)) * kTraceSteps + (step)] = (unsigned long long)clock64(); \
   } while (0)
 #else
-#define FWD_TRACE(ev, step) \
-  do { \
+#define FWD_TRACE(cta, ev, step) \
+  do {                           \
   } while (0)
 #endif
 
@@ -135,33 +135,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_align1024(smem_raw);
   uint8_t* sQ = smem;                               // [2 tiles]
   uint8_t* sRing = sQ + 2 * Cfg::kTile;             // [NS slots]
-  uint8_t* sP = sRing + NS * Cfg::kTile;            // [2 tiles]
+  uint8_t* sP = sRing + NS * Cfg::kTile;            // [2 tiles] (D = 128 only)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (Cfg::kPTmem ? 0 : 2 * Cfg::kPBytes));
   uint64_t* q_full = bars;
-  uint64_t* slot_full = bars + 1;
+  uint64_t* q_empty = bars + 1;        // the S products of an item are done with Q
+  uint64_t* slot_full = bars + 2;
   uint64_t* slot_empty = slot_full + NS;
   uint64_t* s_full = slot_empty + NS;  // [2]
   uint64_t* s_free = s_full + 2;       // [2]
   uint64_t* p_full = s_free + 2;       // [2]
   uint64_t* o_done = p_full + 2;       // [2]
-  uint64_t* done = o_done + 2;
+  uint64_t* o_free = o_done + 2;       // [2] an item's O was read out: the next item's first PV may overwrite it
+  uint64_t* done = o_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int b = bh / a.H, h = bh % a.H;
-  const int m_block = gridDim.x - 1 - blockIdx.x;  // longest (causal) rows first
-  const int m0 = m_block * (2 * BQ);
   const int T = a.T;
   const int kv_blocks = (T + BKV - 1) / BKV;
-  const int nA = a.causal ? min(kv_blocks, m0 / BKV + 1) : kv_blocks;
-  const int nB = a.causal ? min(kv_blocks, m0 / BKV + 2) : kv_blocks;
-  const int row0 = b * T;  // first row of this batch in the [B*T, 3F] matrix
+  const int n_mblocks = (T + 2 * BQ - 1) / (2 * BQ);
+  const int n_items = n_mblocks * a.BH;
+  // work item -> (batch, head, first query row, key blocks of tile A / B);
+  // the longest (causal) query blocks come first in item order
+  struct Item {
+    int bh, b, h, m0, nA, nB, cta;
+  };
+  auto decode = [&](int it) {
+    Item w;
+    const int mb = n_mblocks - 1 - it / a.BH;
+    w.bh = it % a.BH;
+    w.b = w.bh / a.H;
+    w.h = w.bh % a.H;
+    w.m0 = mb * (2 * BQ);
+    w.nA = a.causal ? min(kv_blocks, w.m0 / BKV + 1) : kv_blocks;
+    w.nB = a.causal ? min(kv_blocks, w.m0 / BKV + 2) : kv_blocks;
+    w.cta = n_mblocks - 1 - mb;  // trace index (query blocks from the last)
+    return w;
+  };
 
   constexpr int kProducerWarp = 8, kMmaWarp = 9;
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qkv);
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < NS; ++i) {
       mbar_init(&slot_full[i], 1);
       mbar_init(&slot_empty[i], 1);
@@ -171,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 128);
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -193,29 +209,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kTile);
-      for (int t = 0; t < 2; ++t)
-        for (int kd = 0; kd < KD; ++kd)
-          tma_load_2d(sQ + t * Cfg::kTile + kd * (BQ * 128), &tm_qkv, q_full, (int)(h * D + kd * 64),
-                      row0 + m0 + t * BQ);
-      const int loads = 2 * nB;  // K_0, V_0, K_1, V_1, ...
-      int issued = 0;
-      for (int i = 0; i < loads; ++i) {
-        const int slot = i % NS;
-        const uint32_t use = (uint32_t)(i / NS);
-        if (!mbar_wait_bounded(&slot_empty[slot], (use & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 200)) break;
-        uint8_t* dst = sRing + slot * Cfg::kTile;
-        mbar_arrive_expect_tx(&slot_full[slot], Cfg::kTile);
-        const int col = (int)((i & 1) ? 2 * a.F : a.F) + h * D;
-        const int row = row0 + (i >> 1) * BKV;
-        for (int kd = 0; kd < KD; ++kd)
-          tma_load_2d(dst + kd * (BKV * 128), &tm_qkv, &slot_full[slot], col + kd * 64, row);
-        issued = i + 1;
+      uint32_t L = 0;  // K / V loads issued (ring position, continues across items)
+      uint32_t k = 0;  // items of this CTA
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+        const Item w = decode(it);
+        const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
+        (void)tr_on;
+        // Q of the previous item is no longer read by the tensor core
+        if (!mbar_wait_bounded(q_empty, (k & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 203)) break;
+        FWD_TRACE(w.cta, kTrStart, 0);
+        const int row0 = w.b * T;
+        mbar_arrive_expect_tx(q_full, 2 * Cfg::kTile);
+        for (int t = 0; t < 2; ++t)
+          for (int kd = 0; kd < KD; ++kd)
+            tma_load_2d(sQ + t * Cfg::kTile + kd * (BQ * 128), &tm_qkv, q_full, (int)(w.h * D + kd * 64),
+                        row0 + w.m0 + t * BQ);
+        for (int i = 0; i < 2 * w.nB; ++i, ++L) {  // K_0, V_0, K_1, V_1, ...
+          const uint32_t slot = L % NS, use = L / NS;
+          if (!mbar_wait_bounded(&slot_empty[slot], (use & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 200)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = sRing + slot * Cfg::kTile;
+          mbar_arrive_expect_tx(&slot_full[slot], Cfg::kTile);
+          const int col = (int)((i & 1) ? 2 * a.F : a.F) + w.h * D;
+          const int row = row0 + (i >> 1) * BKV;
+          for (int kd = 0; kd < KD; ++kd)
+            tma_load_2d(dst + kd * (BKV * 128), &tm_qkv, &slot_full[slot], col + kd * 64, row);
+        }
       }
       // drain: every issued copy lands before the CTA exits
-      mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 201);
-      for (int i = (issued > NS ? issued - NS : 0); i < issued; ++i)
-        mbar_wait_bounded(&slot_full[i % NS], (uint32_t)(i / NS) & 1u, a.status, kErrWaitTimeoutFull, 202);
+      if (k > 0) mbar_wait_bounded(q_full, (k - 1) & 1u, a.status, kErrWaitTimeoutFull, 201);
+      for (uint32_t i = (L > (uint32_t)NS ? L - NS : 0); i < L; ++i)
+        mbar_wait_bounded(&slot_full[i % NS], (i / NS) & 1u, a.status, kErrWaitTimeoutFull, 202);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -227,75 +254,94 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t kmaj = make_smem_desc(0, 16, 1024, kSwizzle128B);
       const uint64_t mnmaj = make_smem_desc(0, BKV * 128, 1024, kSwizzle128B);
       const uint32_t q16 = smem_u32(sQ) >> 4, ring16 = smem_u32(sRing) >> 4, p16 = smem_u32(sP) >> 4;
-      auto slot_of = [&](int i) { return (uint32_t)(i % NS); };
-      auto phase_of = [&](int i) { return (uint32_t)(i / NS) & 1u; };
-      auto issue_s = [&](int t, int j) -> bool {
-        if (j > 0 && !mbar_wait_bounded(&s_free[t], (uint32_t)(j - 1) & 1u, a.status, kErrWaitTimeoutAccum, 211))
-          return false;
-        tc_fence_after();
-        const uint64_t ad = kmaj + q16 + t * (Cfg::kTile >> 4);
-        const uint64_t bd = kmaj + ring16 + slot_of(2 * j) * (Cfg::kTile >> 4);
+      uint32_t L = 0;                      // ring position of the current item's K_0
+      uint32_t s_cnt[2] = {0u, 0u};        // S products issued per tile (all items)
+      uint32_t pv_cnt[2] = {0u, 0u};       // PV products issued per tile (all items)
+      uint32_t k = 0;
+      bool ok = true;
+      auto slot_of = [&](uint32_t pos) { return pos % NS; };
+      auto phase_of = [&](uint32_t pos) { return (pos / NS) & 1u; };
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+        const Item w = decode(it);
+        const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
+        (void)tr_on;
+        auto issue_s = [&](int t, int j) -> bool {
+          if (s_cnt[t] > 0 &&
+              !mbar_wait_bounded(&s_free[t], (s_cnt[t] - 1) & 1u, a.status, kErrWaitTimeoutAccum, 211))
+            return false;
+          tc_fence_after();
+          const uint64_t ad = kmaj + q16 + t * (Cfg::kTile >> 4);
+          const uint64_t bd = kmaj + ring16 + slot_of(L + 2 * j) * (Cfg::kTile >> 4);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
-          tc_mma_f16(tmem + Cfg::kSCol + t * BKV, ad + off, bd + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(&s_full[t]);
-        return true;
-      };
-      auto issue_pv = [&](int t, int j) -> bool {
-        if (!mbar_wait_bounded(&p_full[t], (uint32_t)j & 1u, a.status, kErrWaitTimeoutAccum, 212) ||
-            !mbar_wait_bounded(&slot_full[slot_of(2 * j + 1)], phase_of(2 * j + 1), a.status, kErrWaitTimeoutFull,
-                               213))
-          return false;
-        tc_fence_after();
-        const uint64_t ad = kmaj + p16 + t * (Cfg::kPBytes >> 4);
-        const uint64_t bd = mnmaj + ring16 + slot_of(2 * j + 1) * (Cfg::kTile >> 4);
-#pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          if constexpr (Cfg::kPTmem) {
-            // A = P_t from TMEM: keys [16 kk, 16 kk + 16) are columns [8 kk, 8 kk + 8)
-            tc_mma_f16_ts(tmem + Cfg::kOCol + t * D, tmem + Cfg::kPCol + t * (BKV / 2) + (uint32_t)(kk * 8),
-                          bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
-          } else {
-            const uint32_t aoff = ((kk >> 2) * (BQ * 128) + (kk & 3) * 32) >> 4;
-            tc_mma_f16(tmem + Cfg::kOCol + t * D, ad + aoff, bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = ((kk >> 2) * (128 * 128) + (kk & 3) * 32) >> 4;
+            tc_mma_f16(tmem + Cfg::kSCol + t * BKV, ad + off, bd + off, idesc_s, kk > 0 ? 1u : 0u);
           }
-        }
-        tc_commit(&o_done[t]);
-        return true;
-      };
-      bool ok = mbar_wait_bounded(q_full, 0, a.status, kErrWaitTimeoutFull, 210);
-      FWD_TRACE(kTrQFull, 0);
-      // S of block j for both tiles goes ahead of PV of block j-1: a softmax
-      // warpgroup frees S as soon as it holds the row in registers, so the
-      // next S is ready when it finishes P, and the PV product overlaps the
-      // next block's exponentials instead of sitting on the critical path.
-      for (int j = 0; j < nB && ok; ++j) {
-        if (!mbar_wait_bounded(&slot_full[slot_of(2 * j)], phase_of(2 * j), a.status, kErrWaitTimeoutFull, 214)) {
-          ok = false;
-          break;
-        }
-        FWD_TRACE(kTrKFull, j);
-        if ((j < nA && !issue_s(0, j)) || !issue_s(1, j)) {
-          ok = false;
-          break;
-        }
-        tc_commit(&slot_empty[slot_of(2 * j)]);  // K_j read by both tiles
-        FWD_TRACE(kTrIssueS, j);
-        if (j >= 1) {
-          if ((j - 1 < nA && !issue_pv(0, j - 1)) || !issue_pv(1, j - 1)) {
+          tc_commit(&s_full[t]);
+          ++s_cnt[t];
+          return true;
+        };
+        auto issue_pv = [&](int t, int j) -> bool {
+          if (!mbar_wait_bounded(&p_full[t], pv_cnt[t] & 1u, a.status, kErrWaitTimeoutAccum, 212) ||
+              !mbar_wait_bounded(&slot_full[slot_of(L + 2 * j + 1)], phase_of(L + 2 * j + 1), a.status,
+                                 kErrWaitTimeoutFull, 213))
+            return false;
+          // the previous item's O_t must have been read out before this item's first PV overwrites it
+          if (j == 0 && k > 0 && !mbar_wait_bounded(&o_free[t], (k - 1) & 1u, a.status, kErrWaitTimeoutAccum, 216))
+            return false;
+          tc_fence_after();
+          const uint64_t ad = kmaj + p16 + t * (Cfg::kPBytes >> 4);
+          const uint64_t bd = mnmaj + ring16 + slot_of(L + 2 * j + 1) * (Cfg::kTile >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk) {
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (Cfg::kPTmem) {
+              // A = P_t from TMEM: keys [16 kk, 16 kk + 16) are columns [8 kk, 8 kk + 8)
+              tc_mma_f16_ts(tmem + Cfg::kOCol + t * D, tmem + Cfg::kPCol + t * (BKV / 2) + (uint32_t)(kk * 8),
+                            bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
+            } else {
+              const uint32_t aoff = ((kk >> 2) * (BQ * 128) + (kk & 3) * 32) >> 4;
+              tc_mma_f16(tmem + Cfg::kOCol + t * D, ad + aoff, bd + ((kk * 16 * 128) >> 4), idesc_o, acc);
+            }
+          }
+          tc_commit(&o_done[t]);
+          ++pv_cnt[t];
+          return true;
+        };
+        if (!mbar_wait_bounded(q_full, k & 1u, a.status, kErrWaitTimeoutFull, 210)) break;
+        FWD_TRACE(w.cta, kTrQFull, 0);
+        // S of block j for both tiles goes ahead of PV of block j-1: a softmax
+        // warpgroup frees S as soon as it holds the row in registers, so the
+        // next S is ready when it finishes P, and the PV product overlaps the
+        // next block's exponentials instead of sitting on the critical path.
+        for (int j = 0; j < w.nB && ok; ++j) {
+          if (!mbar_wait_bounded(&slot_full[slot_of(L + 2 * j)], phase_of(L + 2 * j), a.status, kErrWaitTimeoutFull,
+                                 214)) {
             ok = false;
             break;
           }
-          tc_commit(&slot_empty[slot_of(2 * (j - 1) + 1)]);  // V_{j-1} read by both tiles
-          FWD_TRACE(kTrIssuePv, j - 1);
+          FWD_TRACE(w.cta, kTrKFull, j);
+          if ((j < w.nA && !issue_s(0, j)) || !issue_s(1, j)) {
+            ok = false;
+            break;
+          }
+          tc_commit(&slot_empty[slot_of(L + 2 * j)]);  // K_j read by both tiles
+          if (j == w.nB - 1) tc_commit(q_empty);        // the item's last S products: Q is free
+          FWD_TRACE(w.cta, kTrIssueS, j);
+          if (j >= 1) {
+            if ((j - 1 < w.nA && !issue_pv(0, j - 1)) || !issue_pv(1, j - 1)) {
+              ok = false;
+              break;
+            }
+            tc_commit(&slot_empty[slot_of(L + 2 * (j - 1) + 1)]);  // V_{j-1} read by both tiles
+            FWD_TRACE(w.cta, kTrIssuePv, j - 1);
+          }
         }
-      }
-      if (ok && nB > 0) {
-        if ((nB - 1 < nA && !issue_pv(0, nB - 1)) || !issue_pv(1, nB - 1)) ok = false;
-        else tc_commit(&slot_empty[slot_of(2 * (nB - 1) + 1)]);
+        if (ok && w.nB > 0) {
+          if ((w.nB - 1 < w.nA && !issue_pv(0, w.nB - 1)) || !issue_pv(1, w.nB - 1)) ok = false;
+          else tc_commit(&slot_empty[slot_of(L + 2 * (w.nB - 1) + 1)]);
+        }
+        L += 2 * w.nB;
       }
       tc_commit(done);
       mbar_wait_bounded(done, 0, a.status, kErrWaitTimeoutAccum, 215);
@@ -306,142 +352,149 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp >> 2;             // tile 0 (A) or 1 (B)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;   // query row within the tile == TMEM lane
-    const int q = m0 + t * BQ + r;
-    const int nblk = t ? nB : nA;
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const uint32_t s_col = lane_base + Cfg::kSCol + t * BKV;
     const uint32_t o_col = lane_base + Cfg::kOCol + t * D;
-    uint8_t* prow = sP + t * Cfg::kPBytes + r * 128;
     const uint32_t p_col = lane_base + Cfg::kPCol + t * (BKV / 2);
-    const int key_limit = a.causal ? min(q + 1, T) : T;  // keys [0, key_limit) are visible
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
+    uint8_t* prow = sP + t * Cfg::kPBytes + r * 128;
     const bool tracer = quarter == 0 && lane == 0;  // warp 0 (tile A) and warp 4 (tile B)
-    if (tracer && t == 0) FWD_TRACE(kTrStart, 0);
-    for (int j = 0; j < nblk && ok; ++j) {
-      if (!mbar_wait_warp(&s_full[t], (uint32_t)j & 1u, a.status, kErrWaitTimeoutAccum, 220)) {
-        ok = false;
-        break;
-      }
-      if (tracer) FWD_TRACE(t == 0 ? kTrSFullA : kTrSFullB, j);
-      tc_fence_after();
-      uint32_t sr[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) tmem_ld_32x32b_x32_async(s_col + c * 32, sr + c * 32);
-      tmem_wait_ld_regs<BKV>(sr);
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);  // S_t may be overwritten by the next block
-      if (tracer && t == 0) FWD_TRACE(kTrSRegsA, j);
-      const int lim = key_limit - j * BKV;  // visible columns of this block: [0, lim)
-      if (lim < BKV) {
-#pragma unroll
-        for (int i = 0; i < BKV; ++i)
-          if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
-      }
-      // row max: four independent chains of three-input max (two scores each)
-      float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]), __uint_as_float(sr[3])};
-#pragma unroll
-      for (int i = 4; i < BKV; i += 8) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          mx4[e] = max3f(mx4[e], __uint_as_float(sr[i + e]), __uint_as_float(sr[i + 4 + e < BKV ? i + 4 + e : i + e]));
-      }
-      const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
-      const float m_blk = mx * a.sl2;
-      const bool rescale = m_blk > m_run + kRescaleThreshold;
-      const float m_new = rescale ? m_blk : m_run;
-      const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.f;  // 0 while m_run = -inf
-      const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      // P = exp2(S * scale * log2e - m): the scale and offset as packed fp32x2
-      // FMAs, the row sum as packed adds into two accumulator pairs
-      float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      const float2 sl2x2 = make_float2(a.sl2, a.sl2), nbase = make_float2(-base, -base);
-      uint32_t pk[BKV / 2];
-#pragma unroll
-      for (int i = 0; i < BKV / 2; ++i) {
-        const float2 x = f2_fma(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2x2, nbase);
-        float2 pr;
-        if ((i & 7) < kPoly) {
-          pr = exp2_poly3_x2(x);
-        } else {
-          pr.x = ex2_approx(x.x);
-          pr.y = ex2_approx(x.y);
-        }
-        rs2[i & 1] = f2_add(rs2[i & 1], pr);
-        pk[i] = pack_bf16x2(pr.x, pr.y);
-      }
-      const float2 rs = f2_add(rs2[0], rs2[1]);
-      l_run = l_run * alpha + (rs.x + rs.y);
-      m_run = m_new;
-      if (tracer && t == 0) FWD_TRACE(kTrExpA, j);
-      // PV(j-1) finished: the P tile is free and O_t holds blocks < j
-      if (j > 0) {
-        if (!mbar_wait_warp(&o_done[t], (uint32_t)(j - 1) & 1u, a.status, kErrWaitTimeoutAccum, 221)) {
+    (void)tracer;
+    uint32_t blk = 0;  // key blocks of this tile processed (all items)
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item w = decode(it);
+      const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
+      (void)tr_on;
+      const int q = w.m0 + t * BQ + r;
+      const int nblk = t ? w.nB : w.nA;
+      const int key_limit = a.causal ? min(q + 1, T) : T;  // keys [0, key_limit) are visible
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < nblk && ok; ++j, ++blk) {
+        if (!mbar_wait_warp(&s_full[t], blk & 1u, a.status, kErrWaitTimeoutAccum, 220)) {
           ok = false;
           break;
         }
+        if (tracer) FWD_TRACE(w.cta, t == 0 ? kTrSFullA : kTrSFullB, j);
         tc_fence_after();
-        if (tracer && t == 0) FWD_TRACE(kTrODoneA, j);
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32_async(o_col + c * 32, ov);
-            tmem_wait_ld_regs<32>(ov);
+        uint32_t sr[BKV];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-            tmem_st_32x32b_x32(o_col + c * 32, ov);
+        for (int c = 0; c < BKV / 32; ++c) tmem_ld_32x32b_x32_async(s_col + c * 32, sr + c * 32);
+        tmem_wait_ld_regs<BKV>(sr);
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // S_t may be overwritten by the next block
+        if (tracer && t == 0) FWD_TRACE(w.cta, kTrSRegsA, j);
+        const int lim = key_limit - j * BKV;  // visible columns of this block: [0, lim)
+        if (lim < BKV) {
+#pragma unroll
+          for (int i = 0; i < BKV; ++i)
+            if (i >= lim) sr[i] = __float_as_uint(-INFINITY);
+        }
+        // row max: four independent chains of three-input max (two scores each)
+        float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]),
+                        __uint_as_float(sr[3])};
+#pragma unroll
+        for (int i = 4; i < BKV; i += 8) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            mx4[e] = max3f(mx4[e], __uint_as_float(sr[i + e]), __uint_as_float(sr[i + 4 + e < BKV ? i + 4 + e : i + e]));
+        }
+        const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
+        const float m_blk = mx * a.sl2;
+        const bool rescale = m_blk > m_run + kRescaleThreshold;
+        const float m_new = rescale ? m_blk : m_run;
+        const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.f;  // 0 while m_run = -inf
+        const float base = (m_new == -INFINITY) ? 0.f : m_new;
+        // P = exp2(S * scale * log2e - m): the scale and offset as packed fp32x2
+        // FMAs, the row sum as packed adds into two accumulator pairs
+        float2 rs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 sl2x2 = make_float2(a.sl2, a.sl2), nbase = make_float2(-base, -base);
+        uint32_t pk[BKV / 2];
+#pragma unroll
+        for (int i = 0; i < BKV / 2; ++i) {
+          const float2 x =
+              f2_fma(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2x2, nbase);
+          float2 pr;
+          if ((i & 7) < kPoly) {
+            pr = exp2_poly3_x2(x);
+          } else {
+            pr.x = ex2_approx(x.x);
+            pr.y = ex2_approx(x.y);
           }
+          rs2[i & 1] = f2_add(rs2[i & 1], pr);
+          pk[i] = pack_bf16x2(pr.x, pr.y);
+        }
+        const float2 rs = f2_add(rs2[0], rs2[1]);
+        l_run = l_run * alpha + (rs.x + rs.y);
+        m_run = m_new;
+        if (tracer && t == 0) FWD_TRACE(w.cta, kTrExpA, j);
+        // PV(j-1) finished: the P tile is free and O_t holds blocks < j
+        if (j > 0) {
+          if (!mbar_wait_warp(&o_done[t], (blk - 1) & 1u, a.status, kErrWaitTimeoutAccum, 221)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (tracer && t == 0) FWD_TRACE(w.cta, kTrODoneA, j);
+          if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tmem_ld_32x32b_x32_async(o_col + c * 32, ov);
+              tmem_wait_ld_regs<32>(ov);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+              tmem_st_32x32b_x32(o_col + c * 32, ov);
+            }
+            tmem_wait_st();
+          }
+        }
+        if constexpr (Cfg::kPTmem) {
+          // P row -> TMEM lane r: column c holds keys 2c, 2c + 1
+          tmem_st_32x32b_x32(p_col, pk);
+          tmem_st_32x32b_x32(p_col + 32, pk + 32);
           tmem_wait_st();
-        }
-      }
-      if constexpr (Cfg::kPTmem) {
-        // P row -> TMEM lane r: column c holds keys 2c, 2c + 1
-        tmem_st_32x32b_x32(p_col, pk);
-        tmem_st_32x32b_x32(p_col + 32, pk + 32);
-        tmem_wait_st();
-      } else {
-        // P row -> swizzled A tile: 16 chunks of 8 keys, chunk ch of sub-tile ch / 8
+        } else {
+          // P row -> swizzled A tile: 16 chunks of 8 keys, chunk ch of sub-tile ch / 8
 #pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
-          const int sub = ch >> 3, c8 = ch & 7;
-          const uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-          *reinterpret_cast<uint4*>(prow + sub * (BQ * 128) + ((c8 ^ (r & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();  // P stores visible to the tensor core
-      }
-      tc_fence_before();  // P / O rescale TMEM stores ordered before the next MMA
-      mbar_arrive(&p_full[t]);
-      if (tracer) FWD_TRACE(t == 0 ? kTrPFullA : kTrPFullB, j);
-    }
-    if (ok && nblk > 0)
-      ok = mbar_wait_warp(&o_done[t], (uint32_t)(nblk - 1) & 1u, a.status, kErrWaitTimeoutAccum, 222);
-    // epilogue: O / l and LSE (TMEM loads in every lane, stores for rows < T)
-    if (tracer && t == 0) FWD_TRACE(kTrEpiStart, 0);
-    if (ok) {
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      __nv_bfloat16* orow = a.o + (long long)(b * T + q) * a.o_stride_t + h * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t ov[32];
-        tmem_ld_32x32b_x32_async(o_col + c * 32, ov);
-        tmem_wait_ld_regs<32>(ov);
-        if (q < T) {
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(ov[g * 8 + 0]) * inv, __uint_as_float(ov[g * 8 + 1]) * inv);
-            v.y = pack_bf16x2(__uint_as_float(ov[g * 8 + 2]) * inv, __uint_as_float(ov[g * 8 + 3]) * inv);
-            v.z = pack_bf16x2(__uint_as_float(ov[g * 8 + 4]) * inv, __uint_as_float(ov[g * 8 + 5]) * inv);
-            v.w = pack_bf16x2(__uint_as_float(ov[g * 8 + 6]) * inv, __uint_as_float(ov[g * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = v;
+          for (int ch = 0; ch < 16; ++ch) {
+            const int sub = ch >> 3, c8 = ch & 7;
+            const uint4 v = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+            *reinterpret_cast<uint4*>(prow + sub * (BQ * 128) + ((c8 ^ (r & 7)) << 4)) = v;
           }
+          fence_proxy_async_smem();  // P stores visible to the tensor core
         }
+        tc_fence_before();  // P / O rescale TMEM stores ordered before the next MMA
+        mbar_arrive(&p_full[t]);
+        if (tracer) FWD_TRACE(w.cta, t == 0 ? kTrPFullA : kTrPFullB, j);
       }
-      if (q < T) a.lse[(long long)bh * T + q] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
+      if (!ok) break;
+      // the item's last PV
+      if (!mbar_wait_warp(&o_done[t], (blk - 1) & 1u, a.status, kErrWaitTimeoutAccum, 222)) break;
+      // epilogue: O / l and LSE (TMEM loads in every lane, stores for rows < T)
+      if (tracer && t == 0) FWD_TRACE(w.cta, kTrEpiStart, 0);
+      tc_fence_after();
+      uint32_t ov[D];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tmem_ld_32x32b_x32_async(o_col + c * 32, ov + c * 32);
+      tmem_wait_ld_regs<D>(ov);
+      tc_fence_before();
+      mbar_arrive(&o_free[t]);  // O_t may be overwritten by the next item
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      if (q < T) {
+        __nv_bfloat16* orow = a.o + (long long)(w.b * T + q) * a.o_stride_t + w.h * D;
+#pragma unroll
+        for (int g = 0; g < D / 8; ++g) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(ov[g * 8 + 0]) * inv, __uint_as_float(ov[g * 8 + 1]) * inv);
+          v.y = pack_bf16x2(__uint_as_float(ov[g * 8 + 2]) * inv, __uint_as_float(ov[g * 8 + 3]) * inv);
+          v.z = pack_bf16x2(__uint_as_float(ov[g * 8 + 4]) * inv, __uint_as_float(ov[g * 8 + 5]) * inv);
+          v.w = pack_bf16x2(__uint_as_float(ov[g * 8 + 6]) * inv, __uint_as_float(ov[g * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + g * 8) = v;
+        }
+        a.lse[(long long)w.bh * T + q] = l_run > 0.f ? m_run + log2f(l_run) : INFINITY;
+      }
+      if (tracer && t == 0) FWD_TRACE(w.cta, kTrEpiEnd, 0);
     }
-    if (tracer && t == 0) FWD_TRACE(kTrEpiEnd, 0);
   }
 
   tc_fence_before();
@@ -487,7 +540,16 @@ void launch_fwd(const AttnParams& p, cudaStream_t s) {
     a.trace_bh = e != nullptr ? atoi(e) : 0;
   }
 #endif
-  dim3 grid((p.T + 2 * BQ - 1) / (2 * BQ), p.B * p.H);
+  a.BH = p.B * p.H;
+  // persistent: one CTA per SM walks the (query block, head) items
+  const long long items = (long long)((p.T + 2 * BQ - 1) / (2 * BQ)) * p.B * p.H;
+  static int sms_by_dev[64] = {0};
+  int dev = 0;
+  UHFS_CUDA_CHECK(cudaGetDevice(&dev));
+  int& sms = sms_by_dev[dev & 63];
+  if (sms == 0) UHFS_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = (int)(items < sms ? items : sms);
+  if (grid <= 0) return;
   fa_fwd_tc_kernel<D, kPoly><<<grid, kThreads, Cfg::kSmem, s>>>(tm, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
