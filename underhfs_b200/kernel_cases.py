@@ -176,7 +176,19 @@ def _case_conv_bwd():
     return lambda: K.conv2d_bwd(dy, x, w, (1, 1), (1, 1), True), 2 * flops, 3 * x.numel() * 4
 
 
+def _torch_mm_case(m: int, n: int, k: int):
+    """Library comparison (not this framework's kernel): torch.matmul bf16,
+    i.e. cuBLAS, on the same shape as the named GEMM case."""
+    def case():
+        a, w = _bf(m, k, scale=0.02), _bf(n, k, scale=0.02)
+        return lambda: torch.matmul(a, w.t()), 2.0 * m * n * k, 0
+    return case
+
+
 CASES: dict[str, Callable] = {
+    "torch_mm_fwd_qkv": _torch_mm_case(TOKENS, 2304, 768),
+    "torch_mm_fc1": _torch_mm_case(TOKENS, 3072, 768),
+    "torch_mm_8192": _torch_mm_case(8192, 8192, 8192),
     "conv_fwd": _case_conv_fwd,
     "conv_bwd": _case_conv_bwd,
     "gemm_fwd": _case_gemm_fwd,
