@@ -55,9 +55,16 @@ def test_stage3_optimizer_tracks_fused_adamw(offload):
     got = model.state_dict(as_tensors=True)  # gathered from the shards
     want = ref.state_dict(as_tensors=True)
     assert set(got) == set(want)
+    # The two paths sum gradients in different orders (fp32 atomics), and Adam
+    # turns tiny differences of near-zero gradients (biases) into visible
+    # update differences: the whole state must agree closely, each parameter
+    # within a bound floored at the size of the three updates.
+    num = sum(((got[n] - want[n]).float() ** 2).sum() for n in want)
+    den = sum((want[n].float() ** 2).sum() for n in want)
+    assert (num / den).sqrt().item() < 1e-2
     for name in want:
-        err = ((got[name] - want[name]).abs().max() / want[name].abs().max().clamp_min(1e-3)).item()
-        assert err < 2e-2, (name, err)
+        err = ((got[name] - want[name]).abs().max() / want[name].abs().max().clamp_min(3 * KW["lr"])).item()
+        assert err < 6e-2, (name, err)
     # backward twice without step() would apply two updates: refused
     model(ids, tg).backward()
     with pytest.raises(RuntimeError, match="optimizer.step"):
