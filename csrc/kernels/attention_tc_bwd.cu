@@ -178,17 +178,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int T = a.T;
   const int i_end = (T + BQ - 1) / BQ;
   const int n_kblocks = (T + BK - 1) / BK;
-  const int n_items = n_kblocks * a.B * a.H;
-  // work item -> (batch, head, key block); key block 0 has the most query
-  // steps under the causal mask, so item order runs from the longest
+  // Work units pair key blocks j and n-1-j of one (batch, head): under the
+  // causal mask every unit has n+1 query steps, so units balance across
+  // CTAs, and units run head-major so that the CTAs working at the same time
+  // share each head's Q / dO tiles in L2.  CTA c takes units c, c+G, c+2G, ...
+  // (G = gridDim.x) and runs both halves of a unit back to back; the virtual
+  // index it = c + m G walks them (half = (it / G) & 1).
+  const int pairs = (n_kblocks + 1) / 2;
+  const int n_units = pairs * a.B * a.H;
+  const int n_virt = 2 * (int)gridDim.x * ((n_units + (int)gridDim.x - 1) / (int)gridDim.x);
   struct Item {
     int bh, b, h, n_block, n0, i_start, steps, row0;
+    bool valid;
   };
   auto decode = [&](int it) {
-    Item w;
-    const int bhs = a.B * a.H;
-    w.n_block = it / bhs;
-    w.bh = it % bhs;
+    Item w{};
+    const int G = gridDim.x;
+    const int u = (it / (2 * G)) * G + it % G;
+    const int hf = (it / G) & 1;
+    const int p = u % pairs;
+    w.bh = u / pairs;
+    w.n_block = hf ? n_kblocks - 1 - p : p;
+    w.valid = u < n_units && !(hf && w.n_block == p);  // an odd count's middle block has no partner
     w.b = w.bh / a.H;
     w.h = w.bh % a.H;
     w.n0 = w.n_block * BK;
@@ -240,15 +251,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;  // query steps of this CTA (all items): ring position
     uint32_t k = 0;  // items of this CTA
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+    for (int it = blockIdx.x; it < n_virt && ok; it += gridDim.x) {
       const Item w = decode(it);
+      if (!w.valid) continue;
       const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
       (void)tr_on;
       const uint32_t kvb = k % KV;
+      ++k;
       int good = 1;
       if (lane == 0) {
         // the MMAs of the item that last used this K / V buffer are done
-        good = mbar_wait_bounded(&kv_empty[kvb], ((k / KV) & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 304);
+        good = mbar_wait_bounded(&kv_empty[kvb], (((k - 1) / KV) & 1u) ^ 1u, a.status, kErrWaitTimeoutEmpty, 304);
         if (good) {
           BWD_TRACE(w.n_block, kTrStart, 0);
           uint8_t* sK = sKV + kvb * 2 * Cfg::kTile;
@@ -331,8 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g0 = 0;  // query steps before the current item
       uint32_t k = 0;
       bool ok = true;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+      for (int it = blockIdx.x; it < n_virt && ok; it += gridDim.x) {
         const Item w = decode(it);
+        if (!w.valid) continue;
         const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
         (void)tr_on;
         const uint32_t kvb = k % KV;
@@ -437,6 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_commit(&kv_empty[kvb]);  // this item's K / V buffer may be refilled
         g0 += w.steps;
+        ++k;
       }
       tc_commit(done);
       mbar_wait_bounded(done, 0, a.status, kErrWaitTimeoutAccum, 316);
@@ -456,8 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool tracer = warp == 0 && lane == 0;
     (void)tracer;
     uint32_t g = 0;  // query steps of this CTA (all items)
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    for (int it = blockIdx.x; it < n_virt; it += gridDim.x) {
       const Item w = decode(it);
+      if (!w.valid) continue;
       const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
       (void)tr_on;
       const int key = w.n0 + r;
@@ -589,8 +605,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int chunk = 0;
     uint32_t g = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    for (int it = blockIdx.x; it < n_virt; it += gridDim.x) {
       const Item w = decode(it);
+      if (!w.valid) continue;
       const bool tr_on = a.trace != nullptr && w.bh == a.trace_bh;
       (void)tr_on;
       for (int tt = 0; tt < w.steps; ++tt, ++g) {
@@ -683,8 +700,8 @@ void launch_bwd(const AttnBwdParams& p, cudaStream_t s) {
     a.trace_bh = e != nullptr ? atoi(e) : 0;
   }
 #endif
-  // persistent: one CTA per SM walks the (key block, head) items
-  const long long items = (long long)((p.f.T + BK - 1) / BK) * p.f.B * p.f.H;
+  // persistent: one CTA per SM walks the units (pairs of key blocks of one head)
+  const long long items = (long long)(((p.f.T + BK - 1) / BK + 1) / 2) * p.f.B * p.f.H;
   static int sms_by_dev[64] = {0};
   int dev = 0;
   UHFS_CUDA_CHECK(cudaGetDevice(&dev));
