@@ -262,15 +262,11 @@ PYBIND11_MODULE(_core, m) {
                           float eps, uintptr_t s) {
     rmsnorm_fwd(dt, P<const void>(x), P<const void>(w), P<void>(y), P<float>(rstd), rows, cols, eps, S(s));
   });
-  m.def(
-      "rmsnorm_bwd",
-      [](int dt, uintptr_t dy, uintptr_t x, uintptr_t w, uintptr_t rstd, uintptr_t dres, uintptr_t dx, uintptr_t dw,
-         int rows, int cols, uintptr_t s, uintptr_t dx_colsum) {
-        rmsnorm_bwd(dt, P<const void>(dy), P<const void>(x), P<const void>(w), P<const float>(rstd),
-                    P<const void>(dres), P<void>(dx), P<float>(dw), rows, cols, S(s), P<float>(dx_colsum));
-      },
-      py::arg("dt"), py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dres"), py::arg("dx"),
-      py::arg("dw"), py::arg("rows"), py::arg("cols"), py::arg("stream"), py::arg("dx_colsum") = 0);
+  m.def("rmsnorm_bwd", [](int dt, uintptr_t dy, uintptr_t x, uintptr_t w, uintptr_t rstd, uintptr_t dres,
+                          uintptr_t dx, uintptr_t dw, int rows, int cols, uintptr_t s) {
+    rmsnorm_bwd(dt, P<const void>(dy), P<const void>(x), P<const void>(w), P<const float>(rstd), P<const void>(dres),
+                P<void>(dx), P<float>(dw), rows, cols, S(s));
+  });
   m.def(
       "embedding_fwd",
       [](int dt, uintptr_t ids, uintptr_t tok, uintptr_t pos, uintptr_t out, int rows, int dim, int seq_len,

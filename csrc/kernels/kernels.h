@@ -24,11 +24,9 @@ void reduce_sum(int dtype, const void* x, long long n, float* out, float* partia
 // ---- RMSNorm (reference nn.py:166-181; here with a real backward)
 void rmsnorm_fwd(int dtype, const void* x, const void* w, void* y, float* rstd, int rows, int cols, float eps,
                  cudaStream_t s);
-// dx = rmsnorm_bwd(dy) (+ dres if dres != null); dw_accum += sum_rows(dy * xhat) (fp32);
-// dx_colsum (optional) += sum_rows(dx) (fp32), the bias gradient of the layer dx belongs to.
+// dx = rmsnorm_bwd(dy) (+ dres if dres != null); dw_accum += sum_rows(dy * xhat) (fp32).
 void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const float* rstd, const void* dres,
-                 void* dx, float* dw_accum, int rows, int cols, cudaStream_t s,
-                 float* dx_colsum = nullptr);
+                 void* dx, float* dw_accum, int rows, int cols, cudaStream_t s);
 
 // ---- embedding (reference nn.py:184-217): token gather + optional learned position
 void embedding_fwd(int dtype, const int64_t* ids, const void* tok, const void* pos, void* out, int rows, int dim,

@@ -184,16 +184,15 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const T* __restr
                                                                 const T* __restrict__ w,
                                                                 const float* __restrict__ rstd,
                                                                 const T* __restrict__ dres, T* __restrict__ dx,
-                                                                float* __restrict__ dw, float* __restrict__ colsum,
-                                                                int rows, int cols) {
+                                                                float* __restrict__ dw, int rows, int cols) {
   __shared__ float part[8][VPL * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float wv[VPL][8], acc[VPL][8], csum[VPL][8];
+  float wv[VPL][8], acc[VPL][8];
 #pragma unroll
   for (int v = 0; v < VPL; ++v) {
     const int c = (v * 32 + lane) * 8;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[v][j] = csum[v][j] = 0.f;
+    for (int j = 0; j < 8; ++j) acc[v][j] = 0.f;
     if (c < cols) unpack8<T>(*reinterpret_cast<const uint4*>(w + c), wv[v]);
     else {
 #pragma unroll
@@ -243,42 +242,22 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const T* __restr
         for (int j = 0; j < 8; ++j) {
           o[j] += r * (a[j] * wv[v][j] - b[j] * coef);
           acc[v][j] = fmaf(a[j] * b[j], r, acc[v][j]);
-          csum[v][j] += o[j];
         }
         __stcs(reinterpret_cast<uint4*>(dx + off + c), pack8<T>(o));
       }
     }
   }
-  // per-column partials of this block's rows: dgamma, then (optionally) the
-  // column sums of dx -- the bias gradient of the layer whose output
-  // gradient dx is -- each combined over the 8 warps in shared memory and
-  // added with one atomic per column
-  if (dw != nullptr) {
+  if (dw == nullptr) return;
 #pragma unroll
-    for (int v = 0; v < VPL; ++v)
+  for (int v = 0; v < VPL; ++v)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) part[warp][(v * 32 + lane) * 8 + j] = acc[v][j];
-    __syncthreads();
-    for (int c = threadIdx.x; c < cols; c += 256) {
-      float sum = 0.f;
+    for (int j = 0; j < 8; ++j) part[warp][(v * 32 + lane) * 8 + j] = acc[v][j];
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += 256) {
+    float sum = 0.f;
 #pragma unroll
-      for (int w8 = 0; w8 < 8; ++w8) sum += part[w8][c];
-      atomicAdd(dw + c, sum);
-    }
-  }
-  if (colsum != nullptr) {
-    __syncthreads();
-#pragma unroll
-    for (int v = 0; v < VPL; ++v)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) part[warp][(v * 32 + lane) * 8 + j] = csum[v][j];
-    __syncthreads();
-    for (int c = threadIdx.x; c < cols; c += 256) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w8 = 0; w8 < 8; ++w8) sum += part[w8][c];
-      atomicAdd(colsum + c, sum);
-    }
+    for (int w8 = 0; w8 < 8; ++w8) sum += part[w8][c];
+    atomicAdd(dw + c, sum);
   }
 }
 
@@ -710,7 +689,7 @@ void rmsnorm_fwd(int dtype, const void* x, const void* w, void* y, float* rstd, 
 }
 
 void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const float* rstd, const void* dres,
-                 void* dx, float* dw_accum, int rows, int cols, cudaStream_t s, float* dx_colsum) {
+                 void* dx, float* dw_accum, int rows, int cols, cudaStream_t s) {
   if (rows <= 0) return;
   const bool vec = al16(dy) && al16(x) && al16(w) && al16(dres) && al16(dx) && (cols % 8 == 0);
   if (vec && dtype != DT_F32 && cols <= 4 * 256) {
@@ -720,7 +699,7 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
     const int vpl = (cols + 255) / 256;
 #define UHFS_RMS_FUSED(TT, V)                                                                                  \
   rmsnorm_bwd_fused_kernel<TT, V><<<grid, 256, 0, s>>>((const TT*)dy, (const TT*)x, (const TT*)w, rstd,         \
-                                                      (const TT*)dres, (TT*)dx, dw_accum, dx_colsum, rows, cols)
+                                                      (const TT*)dres, (TT*)dx, dw_accum, rows, cols)
     if (dtype == DT_BF16) {
       if (vpl == 1) UHFS_RMS_FUSED(__nv_bfloat16, 1);
       else if (vpl == 2) UHFS_RMS_FUSED(__nv_bfloat16, 2);
@@ -737,8 +716,6 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
     UHFS_CUDA_CHECK(cudaGetLastError());
     return;
   }
-  if (dx_colsum != nullptr && dtype != DT_BF16)
-    throw std::invalid_argument("rmsnorm_bwd: the fused dx column sum needs bf16 rows of at most 1024 columns");
   UHFS_DISPATCH_DTYPE(dtype, rmsnorm_bwd_dx_kernel<T><<<row_grid(rows, 8), 256, 0, s>>>(
                                  (const T*)dy, (const T*)x, (const T*)w, rstd, (const T*)dres, (T*)dx, rows, cols, vec));
   note_launch();
@@ -759,7 +736,6 @@ void rmsnorm_bwd(int dtype, const void* dy, const void* x, const void* w, const 
     note_launch();
   }
   UHFS_CUDA_CHECK(cudaGetLastError());
-  if (dx_colsum != nullptr) colsum_accum(static_cast<const __nv_bfloat16*>(dx), cols, dx_colsum, rows, cols, s);
 }
 
 void embedding_fwd(int dtype, const int64_t* ids, const void* tok, const void* pos, void* out, int rows, int dim,

@@ -181,8 +181,6 @@ class LMEngine:
     # defaults so engines that build their own state (ZeRO-3) inherit them
     context_attention = None
     positions: torch.Tensor | None = None
-    # bias gradients of block i-1 may be accumulated during block i's backward
-    cross_block_bias_grads = True
 
     def __init__(self, spec: LMSpec, flat: FlatBuffers, *, causal: bool = True) -> None:
         if spec.features % spec.heads != 0:
@@ -338,15 +336,7 @@ class LMEngine:
         self.unit_backward_begin("tail")
         dhf = K.linear_dgrad(dl, self.Wh)
         K.linear_wgrad_accum(dl, sv["hf"], self.gWh)
-        # the RMSNorm backward that produces a block's output gradient also sums
-        # its columns into that block's fc2 bias gradient when the engine may
-        # accumulate into another block's gradients early (flat buffers, zeroed
-        # once per step); sharded engines zero a unit's gradient slot when its
-        # backward begins, so they take the side-stream column sum instead
-        cross = self.cross_block_bias_grads and bool(self.blocks)
-        dx = K.rmsnorm_backward(dhf, sv["xL"], self.lnf, sv["rf"], None, self.g_lnf,
-                                dx_colsum32=self.blocks[-1]["gb2"] if cross else None)
-        gb2_done = cross
+        dx = K.rmsnorm_backward(dhf, sv["xL"], self.lnf, sv["rf"], None, self.g_lnf)
         self.unit_backward_end("tail")
         if hook is not None and not s.tied:
             hook(*self.tail_range)
@@ -383,17 +373,17 @@ class LMEngine:
             self.unit_backward_begin(bi)
             x, h1, r1, qkv, o, lse, x1, h2, r2, u, g = saved
             # MLP
-            if not gb2_done:
-                colsum_async(dx, blk["gb2"])
+            colsum_async(dx, blk["gb2"])
             du = K.linear_dgrad(dx, blk["W2"], gelu_in=u)
             K.linear_wgrad_accum(dx, g, blk["gW2"])
             colsum_async(du, blk["gb1"])
             dh2 = K.linear_dgrad(du, blk["W1"])
             K.linear_wgrad_accum(du, h2, blk["gW1"])
             del du
-            dx1 = K.rmsnorm_backward(dh2, x1, blk["ln2"], r2, dx, blk["g_ln2"], dx_colsum32=blk["gbo"])
+            dx1 = K.rmsnorm_backward(dh2, x1, blk["ln2"], r2, dx, blk["g_ln2"])
             del dh2
             # attention
+            colsum_async(dx1, blk["gbo"])
             do = K.linear_dgrad(dx1, blk["Wo"])
             K.linear_wgrad_accum(dx1, o, blk["gWo"])
             if self.context_attention is not None:
@@ -405,9 +395,7 @@ class LMEngine:
             dh1 = K.linear_dgrad(dqkv, blk["Wqkv"])
             K.linear_wgrad_accum(dqkv, h1, blk["gWqkv"])
             del dqkv
-            gb2_done = self.cross_block_bias_grads and bi > 0
-            dx = K.rmsnorm_backward(dh1, x, blk["ln1"], r1, dx1, blk["g_ln1"],
-                                    dx_colsum32=self.blocks[bi - 1]["gb2"] if gb2_done else None)
+            dx = K.rmsnorm_backward(dh1, x, blk["ln1"], r1, dx1, blk["g_ln1"])
             del dh1, dx1
             join()
             self.unit_backward_end(bi)

@@ -233,14 +233,11 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> tuple[torch.Tensor,
     return y, rstd
 
 
-def rmsnorm_backward(dy, x, w, rstd, dres=None, dw32=None, dx_colsum32=None):
-    """dx = RMSNorm backward (+ dres); dw32 += dgamma; dx_colsum32 += column
-    sums of dx (the bias gradient of the layer whose output gradient dx is),
-    all in one pass over the rows."""
+def rmsnorm_backward(dy, x, w, rstd, dres=None, dw32=None):
     rows, cols = x.shape
     dx = torch.empty_like(x)
     core().rmsnorm_bwd(dt(x), ptr(dy), ptr(x), ptr(w), ptr(rstd), ptr(dres), ptr(dx), ptr(dw32), rows, cols,
-                       stream(), ptr(dx_colsum32))
+                       stream())
     return dx
 
 

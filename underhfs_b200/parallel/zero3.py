@@ -77,9 +77,6 @@ class Zero3Engine(LMEngine):
     """LMEngine whose weights / gradients are views into gather / gradient
     slots that Zero3LM fills and drains around every unit."""
 
-    # a unit's gradient slot is zeroed when its backward begins
-    cross_block_bias_grads = False
-
     def __init__(self, spec: LMSpec, owner: "Zero3LM", *, causal: bool = True) -> None:
         if spec.head_dim not in (64, 128):
             raise ValueError("the flash-attention kernels support head_dim 64 or 128")
