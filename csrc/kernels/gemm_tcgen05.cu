@@ -28,6 +28,7 @@
 // tile i overlaps the main loop of tile i+1.  Every wait is bounded.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -44,6 +45,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;           // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 352;   // producer, MMA, 8 epilogue warps, pusher (fused all-gather)
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kDefaultStreamKChunk = 0;  // stream-K order: tile-major unless UHFS_STREAMK_CHUNK is set
 
 template <int BN>
 struct GemmCfg {
@@ -68,6 +70,7 @@ struct GemmArgs {
   int M, N, K;
   int tiles_m, tiles_n, splits, kb_per_split, kb_total;
   int stream_k;  // fp32-accumulate only: CTAs take equal contiguous (tile, k-block) ranges
+  int sk_chunk;  // stream-K order: 0 = tile-major; C > 0 = chunks of C k-blocks outermost
   void* C;
   long long ldc;
   const __nv_bfloat16* bias;
@@ -121,7 +124,11 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, i
 //   stream-K: the k-block range [idx*W/cnt, (idx+1)*W/cnt) of the
 //             W = tiles * kb_total linearised (tile, k-block) space, cut at
 //             tile boundaries; each piece is accumulated into C by the fp32
-//             epilogue.
+//             epilogue.  With sk_chunk = C the space is ordered (k-chunk of
+//             C k-blocks, tile, k-block): the CTAs running at the same time
+//             then cover the same k-range of many tiles, so the A rows and
+//             B columns of that range are shared in L2 instead of each CTA
+//             streaming a different k-range of one tile.
 struct UnitIter {
   long long pos, end;
   int stride;
@@ -139,9 +146,22 @@ __device__ __forceinline__ bool unit_next(const GemmArgs& a, UnitIter& it, int& 
   if (it.pos >= it.end) return false;
   int split;
   if (a.stream_k) {
-    const int tile = (int)(it.pos / a.kb_total);
-    kb0 = (int)(it.pos - (long long)tile * a.kb_total);
-    kb1 = (int)min((long long)a.kb_total, kb0 + (it.end - it.pos));
+    int tile;
+    if (a.sk_chunk > 0) {
+      const long long tiles = (long long)a.tiles_m * a.tiles_n;
+      const long long per_chunk = tiles * a.sk_chunk;
+      const long long c = it.pos / per_chunk;
+      const int chunk_lo = (int)(c * a.sk_chunk);
+      const int chunk_len = min(a.sk_chunk, a.kb_total - chunk_lo);
+      const long long rem = it.pos - c * per_chunk;
+      tile = (int)(rem / chunk_len);
+      kb0 = chunk_lo + (int)(rem - (long long)tile * chunk_len);
+      kb1 = (int)min((long long)(chunk_lo + chunk_len), kb0 + (it.end - it.pos));
+    } else {
+      tile = (int)(it.pos / a.kb_total);
+      kb0 = (int)(it.pos - (long long)tile * a.kb_total);
+      kb1 = (int)min((long long)a.kb_total, kb0 + (it.end - it.pos));
+    }
     it.pos += kb1 - kb0;
     tile_coords(a, tile, tm, tn, split);
     return true;
@@ -891,6 +911,17 @@ CUtensorMap make_tmap(const void* base, uint64_t inner, uint64_t outer, uint64_t
   return m;
 }
 
+// UHFS_STREAMK_CHUNK: k-blocks per chunk of the chunk-major stream-K order
+// (0 = tile-major).
+int stream_k_chunk() {
+  static const int c = [] {
+    const char* e = getenv("UHFS_STREAMK_CHUNK");
+    const int v = e != nullptr ? atoi(e) : kDefaultStreamKChunk;
+    return v > 0 ? v : 0;
+  }();
+  return c;
+}
+
 int num_sms() {
   static int by_dev[64] = {0};
   int dev = 0;
@@ -940,6 +971,7 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   a.kb_total = (p.K + BK - 1) / BK;
   // splits == 0 with the fp32-accumulate epilogue selects stream-K
   a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
+  a.sk_chunk = a.stream_k ? stream_k_chunk() : 0;
   int splits = p.splits < 1 ? 1 : p.splits;
   if (splits > a.kb_total) splits = a.kb_total;
   a.kb_per_split = (a.kb_total + splits - 1) / splits;
@@ -1044,6 +1076,7 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   a.kb_per_split = a.kb_total;
   // splits == 0 with the fp32-accumulate epilogue selects stream-K over pairs
   a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
+  a.sk_chunk = a.stream_k ? stream_k_chunk() : 0;
   a.C = p.C;
   a.ldc = p.ldc;
   a.bias = p.bias;
