@@ -54,6 +54,8 @@ CONFIGS = {
                      desc="7B TransformerLM (d_model 4096, 32 layers, 32 heads, MLP 11008, vocab 32000, untied)"),
     # the CPU-fallback configuration: the one the reference's own runtime can
     # complete (pure Python, about 2.2-2.5 tokens/s on an 8-core host)
+    # element-wise add / mul at 2^26, GEMM at 1024/4096/8192, collectives at N > 1
+    "micro": dict(model=None, batch=0, seq=0, zero=0, desc="microbenchmarks"),
     "tiny-cpu": dict(model="tiny", batch=8, seq=64, zero=0, cpu=True,
                      desc="tiny TransformerLM (byte vocab 256, d_model 64, 2 blocks, 4 heads, MLP 256), CPU"),
 }
@@ -622,6 +624,182 @@ def run_zero3(args, pol, cc) -> int:
     return 0
 
 
+_REF_MICRO = """
+import json, statistics, sys, time
+from underhfs import _core as core
+
+iters, warm, with_coll = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3] == "1"
+
+def wall(fn):
+    for _ in range(warm):
+        fn()
+    ts = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
+
+def emit(**kw):
+    print(json.dumps(kw), flush=True)
+
+if not with_coll:
+    n = 1 << 26
+    for cls, name, es in (("CudaTensorF32", "fp32", 4), ("CudaTensorF16", "fp16", 2), ("CudaTensorBF16", "bf16", 2)):
+        C = getattr(core, cls)
+        a, b = C([1.5] * n, [n]), C([2.5] * n, [n])
+        for op in ("add", "mul"):
+            f = getattr(a, op)
+            t = wall(lambda: f(b))
+            emit(op=op, dtype=name, numel=n, seconds=t, gbs=3 * n * es / t / 1e9)
+        del a, b
+    for m in (1024, 4096, 8192):
+        a, b = core.CudaTensorF32([1.0] * (m * m), [m, m]), core.CudaTensorF32([0.5] * (m * m), [m, m])
+        t = wall(lambda: a.matmul(b))
+        emit(op="matmul", dtype="fp32", m=m, n=m, k=m, seconds=t, tflops=2.0 * m ** 3 / t / 1e12)
+        del a, b
+    from underhfs.benchmarks import run_microbenchmarks
+    for r in run_microbenchmarks(size=32, iterations=iters, warmup=warm, include_cuda=True):
+        emit(op="run_microbenchmarks", **r.to_dict())
+else:
+    rank, world, uid, max_bytes = int(sys.argv[4]), int(sys.argv[5]), sys.argv[6], int(sys.argv[7])
+    pg = core.NcclProcessGroup(rank, world, uid)
+    nbytes = 1024
+    while nbytes <= max_bytes:
+        count = nbytes // 4 // world * world
+        vec = [1.0] * count
+        for op, fn in (("all_reduce_sum", lambda: pg.all_reduce_sum(vec)),
+                       ("reduce_scatter", lambda: pg.reduce_scatter(vec)),
+                       ("all_gather", lambda: pg.all_gather(vec[: count // world]))):
+            pg.barrier()
+            t = wall(fn)
+            emit(op=op, bytes=count * 4, seconds=t, rank=rank)
+        nbytes *= 4
+"""
+
+
+def run_reference_micro(args) -> int:
+    """The reference's own microbenchmarks on its stock native module (the
+    collectives/GEMM/elementwise configuration): CudaTensor{F32,F16,BF16}
+    add / mul at 2^26 elements, the cublasSgemm matmul at 1024/4096/8192 and,
+    with N > 1 ranks, NcclProcessGroup all_reduce_sum / reduce_scatter /
+    all_gather from 1 KiB up (host vectors in and out, as its API takes
+    them), plus its ``run_microbenchmarks`` suite.  Every op of that API
+    synchronises its stream before returning, so the time is the host wall
+    clock around the call (median).  Runs in a subprocess rooted at
+    baseline/_ref; each rank's subprocess sees only its own GPU
+    (CUDA_VISIBLE_DEVICES), since the reference selects no device itself.
+    Reference: benchmarks.py:98-120, cuda/kernels.cu:428-500,
+    cpp/nccl_runtime.cpp:120-170."""
+    ref = ROOT / "baseline" / "_ref"
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not (ref / "underhfs" / "__init__.py").exists():
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "config": "micro",
+                              "unavailable": "reference not installed under baseline/_ref"}))
+        return 0
+    env = dict(os.environ, PYTHONPATH=str(ref), CUDA_VISIBLE_DEVICES=str(local))
+    iters, warm = (args.steps if args.steps_given else 10), args.warmup
+    rows = []
+
+    def run(argv, timeout):
+        proc = subprocess.run([sys.executable, "-c", _REF_MICRO, *map(str, argv)], cwd=str(ref), env=env,
+                              capture_output=True, text=True, timeout=timeout)
+        out = [json.loads(l) for l in proc.stdout.splitlines() if l.startswith("{")]
+        if proc.returncode != 0:
+            out.append({"error": (proc.stderr.strip().splitlines() or ["?"])[-1]})
+        return out
+
+    if rank == 0:
+        rows += run([iters, warm, 0], 900)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+        uid = [None]
+        if rank == 0:
+            uid[0] = subprocess.run([sys.executable, "-c", "from underhfs import _core; print(_core.nccl_create_unique_id_hex())"],
+                                    cwd=str(ref), env=env, capture_output=True, text=True).stdout.strip()
+        dist.broadcast_object_list(uid, src=0)
+        max_bytes = int(os.environ.get("UNDERHFS_REF_COLL_MAX_BYTES", str(64 << 20)))
+        coll = run([iters, warm, 1, rank, world, uid[0], max_bytes], 1800)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, coll)
+        dist.destroy_process_group()
+        if rank == 0:
+            by_key = {}
+            for per_rank in gathered:
+                for r in per_rank:
+                    if "op" in r:
+                        k = (r["op"], r["bytes"])
+                        by_key[k] = max(by_key.get(k, 0.0), r["seconds"])
+                    else:
+                        rows.append(r)
+            for (op, nbytes), t in sorted(by_key.items()):
+                # bus bandwidth over the full vector (the gathered output for all_gather)
+                busbw = {"all_reduce_sum": 2.0 * (world - 1) / world}.get(op, (world - 1) / world)
+                rows.append({"op": op, "dtype": "fp32", "bytes": nbytes, "n_gpus": world, "seconds": t,
+                             "bus_gbs": busbw * nbytes / t / 1e9})
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(dict({"impl": "reference", "config": "micro",
+                                   "timer": "host wall clock around the synchronous call, median"}, **r)))
+    return 0
+
+
+def run_micro(args) -> int:
+    """This framework on the same microbenchmarks: element-wise add / mul at
+    2^26 elements (fp32, fp16, bf16), GEMM at 1024/4096/8192 (the tcgen05
+    bf16 GEMM, and the exact fp32 SIMT GEMM for a like-for-like fp32 row),
+    device time with CUDA events (mean after warm-up; inputs larger than L2
+    for the element-wise ops); with N > 1 ranks the collective sweep
+    (P2P all-reduce / reduce-scatter / all-gather over NVLink against NCCL)."""
+    import torch
+
+    from underhfs_b200.ops import kernels as K
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        from underhfs_b200.parallel import collective_bench
+
+        return collective_bench.main(["--min-kib", "1", "--max-mib", "1024", "--step", "4"])
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    iters = args.steps if args.steps_given else 20
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / iters
+
+    n = 1 << 26
+    for dtype, name in ((torch.float32, "fp32"), (torch.float16, "fp16"), (torch.bfloat16, "bf16")):
+        a = torch.full((n,), 1.5, dtype=dtype, device=dev)
+        b = torch.full((n,), 2.5, dtype=dtype, device=dev)
+        for op, code in (("add", K.OP_ADD), ("mul", K.OP_MUL)):
+            t = timed(lambda: K.ew_binary(code, a, b))
+            print(json.dumps({"impl": "ours", "config": "micro", "op": op, "dtype": name, "numel": n, "seconds": t,
+                              "gbs": 3 * n * a.element_size() / t / 1e9, "timer": "CUDA events"}))
+        del a, b
+    for m in (1024, 4096, 8192):
+        for dtype, name, fn in ((torch.bfloat16, "bf16", K.matmul_bf16), (torch.float32, "fp32", K.matmul_f32)):
+            a = torch.randn(m, m, device=dev).to(dtype)
+            b = torch.randn(m, m, device=dev).to(dtype)
+            t = timed(lambda: fn(a, b))
+            print(json.dumps({"impl": "ours", "config": "micro", "op": "matmul", "dtype": name, "m": m, "n": m, "k": m,
+                              "seconds": t, "tflops": 2.0 * m ** 3 / t / 1e12, "timer": "CUDA events"}))
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
@@ -636,6 +814,10 @@ def main() -> int:
                     help="125m-ddp is the headline run; the sharded configurations are measured the same way")
     args = ap.parse_args()
     args.steps_given = "--steps" in sys.argv
+    if args.config == "micro":
+        if "--warmup" not in sys.argv:
+            args.warmup = 3
+        return run_reference_micro(args) if args.impl == "reference" else run_micro(args)
     if args.config == "tiny-cpu":
         if "--warmup" not in sys.argv:
             args.warmup = 3
