@@ -307,20 +307,20 @@ def trace_attn_fwd(ctas=(0, 2)) -> str:
 
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("case", choices=sorted(CASES) + ["all"])
+    ap.add_argument("case", nargs="+", choices=sorted(CASES) + ["all"], help="one or more cases, or all")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="print CUDA-event time per launch")
     ap.add_argument("--trace", action="store_true", help="attn_bwd: print the kernel's per-step clock stamps")
     args = ap.parse_args(argv)
     torch.manual_seed(0)
     if args.trace:
-        if args.case not in ("attn_bwd", "attn_fwd"):
+        if len(args.case) != 1 or args.case[0] not in ("attn_bwd", "attn_fwd"):
             ap.error("--trace is available for attn_fwd and attn_bwd")
-        print(trace_attn_bwd() if args.case == "attn_bwd" else trace_attn_fwd())
+        print(trace_attn_bwd() if args.case[0] == "attn_bwd" else trace_attn_fwd())
         st = K.core().device_status(True)
         print("ok" if st["code"] == 0 else f"device status {st}")
         return 0 if st["code"] == 0 else 1
-    names = sorted(CASES) if args.case == "all" else [args.case]
+    names = sorted(CASES) if "all" in args.case else args.case
     for name in names:
         fn, flops, nbytes = CASES[name]()
         if args.time:
