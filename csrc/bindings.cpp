@@ -235,6 +235,11 @@ PYBIND11_MODULE(_core, m) {
   m.def("gemm_f32", [](uintptr_t A, uintptr_t B, uintptr_t C, int M, int N, int K, bool b_trans, uintptr_t s) {
     gemm_f32_simt(P<const float>(A), P<const float>(B), P<float>(C), M, N, K, b_trans, S(s));
   });
+  m.def("gemm_f32_3xtf32", [](uintptr_t A, uintptr_t B, uintptr_t C, int M, int N, int K, bool b_trans, uintptr_t ws_a,
+                              uintptr_t ws_b, uintptr_t s) {
+    gemm_f32_3xtf32(P<const float>(A), P<const float>(B), P<float>(C), M, N, K, b_trans, P<float>(ws_a), P<float>(ws_b),
+                    S(s));
+  });
   m.def("ew_binary", [](int op, int dt, uintptr_t a, uintptr_t b, uintptr_t out, long long n, uintptr_t s) {
     ew_binary(op, dt, P<const void>(a), P<const void>(b), P<void>(out), n, S(s));
   });

@@ -71,6 +71,20 @@ struct GemmProblem {
 
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream);
 
+// fp32 C[M,N] (row stride ldc) = A[M,K] B[N,K]^T with tf32 tensor-core math
+// (both operands K-major fp32, rows 16-byte aligned, strides multiples of 4).
+void gemm_tf32_tcgen05(const float* A, long long lda, const float* B, long long ldb, float* C, long long ldc, int M,
+                       int N, int K, cudaStream_t stream);
+
+// fp32 C[M,N] = A[M,K] x B (b_trans=false -> B[K,N], true -> B[N,K]) as three
+// tf32 tensor-core products per term (3xTF32): x = hi + lo with hi the tf32
+// rounding of x, and C = hi(A) lo(B) + lo(A) hi(B) + hi(A) hi(B), accumulated
+// in fp32 -- one GEMM over operands concatenated along K.  The workspaces hold
+// the split operands: ws_a M x 3Kp floats, ws_b N x 3Kp floats, Kp = K rounded
+// up to 32.
+void gemm_f32_3xtf32(const float* A, const float* B, float* C, int M, int N, int K, bool b_trans, float* ws_a,
+                     float* ws_b, cudaStream_t stream);
+
 // C[M,N] (fp32) = A[M,K] (fp32, row-major) x B (fp32): b_trans=false -> B[K,N], true -> B[N,K].
 // Exact fp32 FMA accumulation (the fp32 contract of the public matmul).
 void gemm_f32_simt(const float* A, const float* B, float* C, int M, int N, int K, bool b_trans, cudaStream_t stream);

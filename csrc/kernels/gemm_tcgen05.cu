@@ -71,6 +71,8 @@ struct GemmArgs {
   int tiles_m, tiles_n, splits, kb_per_split, kb_total;
   int stream_k;  // fp32-accumulate only: CTAs take equal contiguous (tile, k-block) ranges
   int sk_chunk;  // stream-K order: 0 = tile-major; C > 0 = chunks of C k-blocks outermost
+  int group;     // grouped raster: M-tiles walked down a column of N before moving right
+  int k_chunk;   // > 0: each tile as consecutive units of k_chunk k-blocks on one CTA (pair)
   void* C;
   long long ldc;
   const __nv_bfloat16* bias;
@@ -132,6 +134,7 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, i
 struct UnitIter {
   long long pos, end;
   int stride;
+  int chunk = 0;  // k_chunk mode: next chunk of tile `pos`
 };
 
 __device__ __forceinline__ UnitIter unit_begin(const GemmArgs& a, int idx, int cnt) {
@@ -166,6 +169,19 @@ __device__ __forceinline__ bool unit_next(const GemmArgs& a, UnitIter& it, int& 
     tile_coords(a, tile, tm, tn, split);
     return true;
   }
+  if (a.k_chunk > 0) {
+    // tiles idx, idx + cnt, ..., each as its k-chunks in order on this CTA
+    tile_coords(a, (int)it.pos, tm, tn, split);
+    kb0 = it.chunk * a.k_chunk;
+    kb1 = min(kb0 + a.k_chunk, a.kb_total);
+    if (kb1 >= a.kb_total) {
+      it.chunk = 0;
+      it.pos += it.stride;
+    } else {
+      ++it.chunk;
+    }
+    return true;
+  }
   tile_coords(a, (int)it.pos, tm, tn, split);
   kb0 = split * a.kb_per_split;
   kb1 = min(kb0 + a.kb_per_split, a.kb_total);
@@ -177,9 +193,9 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tm, i
   const int mn_tiles = a.tiles_m * a.tiles_n;
   split = t / mn_tiles;
   int mn = t - split * mn_tiles;
-  // Grouped raster: walk 16 M-tiles down a column of N before moving right,
-  // so concurrently running CTAs share B tiles in L2.
-  constexpr int G = 16;
+  // Grouped raster: walk `group` M-tiles down a column of N before moving
+  // right, so concurrently running CTAs share B tiles in L2.
+  const int G = a.group;
   const int group_span = G * a.tiles_n;
   const int g = mn / group_span;
   const int first_m = g * G;
@@ -669,14 +685,19 @@ __host__ __device__ constexpr int pair_smem_bytes(int epi) {
   return 1024 + pair_stages(epi) * kPairStageBytes + pair_box_bytes(epi) + 256;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+// TF32: operands are fp32 (tf32 math, kind::tf32), K-major both, fp32 store
+// epilogue; a k-block is then 32 elements (the same 128-byte rows), and an
+// MMA of K = 8 covers the 32 bytes a bf16 MMA of K = 16 does.
+template <bool A_MN, bool B_MN, int EPI, bool TF32 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAuxOut,
                      const GemmArgs args) {
+  static_assert(!TF32 || (!A_MN && !B_MN && EPI == GEMM_EPI_F32_STORE), "tf32: K-major operands, fp32 store");
   constexpr int S = pair_stages(EPI);
   constexpr int kABytes = kPairHalf * BK * 2;
-  constexpr uint32_t kIdesc = make_idesc(1 /*bf16*/, A_MN ? 1 : 0, B_MN ? 1 : 0, 2 * kPairHalf, 2 * kPairHalf);
+  constexpr int kKElems = TF32 ? BK / 2 : BK;  // elements of K per k-block (128 bytes)
+  constexpr uint32_t kIdesc = make_idesc(TF32 ? 2 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0, 2 * kPairHalf, 2 * kPairHalf);
   constexpr int kBoxes = epi_boxes(EPI);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);  // same offsets in both CTAs
@@ -744,7 +765,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           uint8_t* sB = sA + kABytes;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
           const uint32_t bar = full_leader + stage * 8;
-          const int k0 = kb * BK;
+          const int k0 = kb * kKElems;
           if constexpr (!A_MN) {
             tma_load_2d_pair(sA, &tmA, bar, k0, m0);
           } else {
@@ -808,7 +829,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 bdesc = make_smem_desc(b_base + kk * 32, 16, 1024, kSwizzle128B);
               else
                 bdesc = make_smem_desc(b_base + kk * 16 * 128, 64 * BK * 2, 1024, kSwizzle128B);
-              tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              if constexpr (TF32)
+                tc_mma_tf32_pair(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              else
+                tc_mma_f16_pair(d_tmem, adesc, bdesc, kIdesc, (kb > kb0 || kk > 0) ? 1u : 0u);
             }
             // frees this stage in both CTAs once the MMAs retire
             tc_commit_pair(empty_l + stage * 8);
@@ -821,7 +845,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           if (!ok) break;
           tc_commit_pair(tfull_l + acc * 8);
           tc_commit_pair(tfull_p + acc * 8);
-          if (++acc == 2) {
+          if (TF32) {
+            acc_phase ^= 1u;  // one partial accumulator; the other holds the running sum
+          } else if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
           }
@@ -845,6 +871,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint32_t seq = 0;
     UnitIter it = unit_begin(args, (int)cluster_id_x(), (int)cluster_count_x());
     int tm, tn, kb0, kb1;
+    if constexpr (TF32) {
+      // The tensor core's fp32 accumulation is not round-to-nearest, so its
+      // error grows with the number of MMA steps summed in TMEM.  A tile is
+      // therefore accumulated in chunks of k_chunk k-blocks into TMEM columns
+      // [0, 256); the epilogue adds each chunk (round-to-nearest, CUDA cores)
+      // into a running sum in columns [256, 512) and writes the tile after
+      // its last chunk.
+      const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+      while (unit_next(args, it, tm, tn, kb0, kb1)) {
+        const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf, n0 = tn * 2 * kPairHalf;
+        if (!mbar_wait_warp_cluster(&tfull[0], acc_phase, args.status, kErrWaitTimeoutAccum, 31)) break;
+        tc_fence_after();
+        const bool first = kb0 == 0, last = kb1 >= args.kb_total;
+        const int r = m0 + quarter * 32 + lane;
+        float* dst = reinterpret_cast<float*>(args.C) + (long long)r * args.ldc;
+#pragma unroll 1
+        for (int j = 0; j < kPairHalf / 32; ++j) {
+          const uint32_t col = (uint32_t)((ehalf * (kPairHalf / 32) + j) * 32);
+          float v[32];
+          tmem_ld_32x32b_x32(lane_base + col, v);
+          if (!first) {
+            float sum[32];
+            tmem_ld_32x32b_x32(lane_base + 2 * kPairHalf + col, sum);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += sum[i];
+          }
+          if (!last) {
+            uint32_t bits[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) bits[i] = __float_as_uint(v[i]);
+            tmem_st_32x32b_x32(lane_base + 2 * kPairHalf + col, bits);
+          } else if (r < args.M) {
+            const int col0 = n0 + (int)col;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (col0 + q * 4 < args.N)
+                *reinterpret_cast<float4*>(dst + col0 + q * 4) =
+                    make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader);  // the partial accumulator may be overwritten
+        acc_phase ^= 1u;
+      }
+    } else
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * 2 * kPairHalf + (int)rank * kPairHalf, n0 = tn * 2 * kPairHalf;
       AuxRegs<2 * kPairHalf> aux;
@@ -911,6 +984,36 @@ CUtensorMap make_tmap(const void* base, uint64_t inner, uint64_t outer, uint64_t
   return m;
 }
 
+// 2-D fp32 tensor map, 128-byte swizzle, box {32, box_outer} (128-byte rows).
+CUtensorMap make_tmap_f32(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                          uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("gemm operand must be 16-byte aligned");
+  if ((row_stride_elems * 4) % 16 != 0) throw std::runtime_error("fp32 gemm leading dimension must be a multiple of 4");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 4};
+  cuuint32_t box[2] = {32, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+// UHFS_GEMM_GROUP: M-tiles per raster group.  8 measured best on the 125M
+// step (1,059,248 tokens/s against 1,036,639 with 16; 4 and 32 slower at
+// 8192^3).
+constexpr int kDefaultRasterGroup = 8;
+int raster_group() {
+  static const int g = [] {
+    const char* e = getenv("UHFS_GEMM_GROUP");
+    const int v = e != nullptr ? atoi(e) : kDefaultRasterGroup;
+    return v > 0 ? v : kDefaultRasterGroup;
+  }();
+  return g;
+}
+
 // UHFS_STREAMK_CHUNK: k-blocks per chunk of the chunk-major stream-K order
 // (0 = tile-major).
 int stream_k_chunk() {
@@ -962,7 +1065,7 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   // A: K-major [M][lda] -> dims {K, M}; MN-major [K][lda] -> dims {M, K}
   CUtensorMap ta = A_MN ? make_tmap(p.A, p.M, p.K, p.lda, BK) : make_tmap(p.A, p.K, p.M, p.lda, BM);
   CUtensorMap tb = B_MN ? make_tmap(p.B, p.N, p.K, p.ldb, BK) : make_tmap(p.B, p.K, p.N, p.ldb, BN);
-  GemmArgs a;
+  GemmArgs a = {};
   a.M = p.M;
   a.N = p.N;
   a.K = p.K;
@@ -972,6 +1075,7 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   // splits == 0 with the fp32-accumulate epilogue selects stream-K
   a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
   a.sk_chunk = a.stream_k ? stream_k_chunk() : 0;
+  a.group = raster_group();
   int splits = p.splits < 1 ? 1 : p.splits;
   if (splits > a.kb_total) splits = a.kb_total;
   a.kb_per_split = (a.kb_total + splits - 1) / splits;
@@ -1077,6 +1181,7 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   // splits == 0 with the fp32-accumulate epilogue selects stream-K over pairs
   a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
   a.sk_chunk = a.stream_k ? stream_k_chunk() : 0;
+  a.group = raster_group();
   a.C = p.C;
   a.ldc = p.ldc;
   a.bias = p.bias;
@@ -1092,6 +1197,52 @@ void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   if constexpr (epi_boxes(EPI) > 0) tc = make_out_tmap(p.C, p.N, p.M, p.ldc);
   if constexpr (epi_boxes(EPI) > 1) taux = make_out_tmap(p.aux_out, p.N, p.M, p.ld_aux_out);
   kern<<<2 * ncl, kPairThreads, kSmem, stream>>>(ta, tb, tc, taux, a);
+  note_launch();
+  UHFS_CUDA_CHECK(cudaGetLastError());
+}
+
+// k-blocks (32 tf32 elements each, 4 MMAs of K = 8) accumulated in TMEM
+// before the epilogue folds them into the round-to-nearest running sum
+constexpr int kTf32ChunkKb = 16;
+
+// fp32 C[M, N] = A[M, K] B[N, K]^T on the tensor cores in tf32 (K-major fp32
+// operands, CTA pairs, 256 x 256 tiles).  The 3xTF32 fp32 GEMM calls it on
+// operands split into tf32 high and low parts.
+void gemm_tf32_pair(const float* A, long long lda, const float* B, long long ldb, float* C, long long ldc, int M,
+                    int N, int K, cudaStream_t stream) {
+  constexpr int EPI = GEMM_EPI_F32_STORE;
+  constexpr int kSmem = pair_smem_bytes(EPI);
+  auto kern = gemm_pair_kernel<false, false, EPI, true>;
+  static int clusters_by_dev[64] = {0};
+  static PerDeviceOnce once;
+  int dev = 0;
+  UHFS_CUDA_CHECK(cudaGetDevice(&dev));
+  once([&] {
+    UHFS_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    clusters_by_dev[dev & 63] = max_pair_clusters(kern, kSmem);
+  });
+  if (ldc % 4 != 0) throw std::runtime_error("tf32 gemm: ldc must be a multiple of 4");
+  const int clusters = clusters_by_dev[dev & 63];
+  CUtensorMap ta = make_tmap_f32(A, K, M, lda, kPairHalf);
+  CUtensorMap tb = make_tmap_f32(B, K, N, ldb, kPairHalf);
+  GemmArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.tiles_m = (M + 2 * kPairHalf - 1) / (2 * kPairHalf);
+  a.tiles_n = (N + 2 * kPairHalf - 1) / (2 * kPairHalf);
+  a.kb_total = (K + BK / 2 - 1) / (BK / 2);
+  a.group = raster_group();
+  a.k_chunk = kTf32ChunkKb;
+  a.splits = 1;
+  a.kb_per_split = a.kb_total;
+  a.C = C;
+  a.ldc = ldc;
+  a.status = device_status_ptr();
+  const long long units = (long long)a.tiles_m * a.tiles_n;
+  const int ncl = units < clusters ? (int)units : clusters;
+  CUtensorMap unused{};
+  kern<<<2 * ncl, kPairThreads, kSmem, stream>>>(ta, tb, unused, unused, a);
   note_launch();
   UHFS_CUDA_CHECK(cudaGetLastError());
 }
@@ -1182,6 +1333,13 @@ CUtensorMap make_tmap_f32_2d(const void* base, uint64_t inner, uint64_t outer, u
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return m;
+}
+
+void gemm_tf32_tcgen05(const float* A, long long lda, const float* B, long long ldb, float* C, long long ldc, int M,
+                       int N, int K, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return;
+  if (K <= 0) throw std::runtime_error("tf32 gemm: K must be positive");
+  gemm_tf32_pair(A, lda, B, ldb, C, ldc, M, N, K, stream);
 }
 
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream) {

@@ -43,6 +43,16 @@ def _case_gemm_fwd_gelu():
     return lambda: K.linear_fwd_gelu(x, w, b), 2.0 * TOKENS * 3072 * 768, 0
 
 
+def _resid_case(n_out: int, n_in: int):
+    """Linear with bias and the residual add fused in the epilogue (the
+    out-projection is 768 x 768, fc2 768 x 3072)."""
+    def case():
+        x, w, b, r = _bf(TOKENS, n_in), _bf(n_out, n_in, scale=0.03), _bf(n_out), _bf(TOKENS, n_out)
+        out = torch.empty(TOKENS, n_out, dtype=torch.bfloat16, device="cuda")
+        return lambda: K.linear_fwd_resid(x, w, b, r, out=out), 2.0 * TOKENS * n_out * n_in, 0
+    return case
+
+
 def _case_gemm_dgrad_dgelu():
     dy, w, u = _bf(TOKENS, 768), _bf(768, 3072, scale=0.03), _bf(TOKENS, 3072)
     return lambda: K.linear_dgrad(dy, w, gelu_in=u), 2.0 * TOKENS * 3072 * 768, 0
@@ -194,6 +204,8 @@ CASES: dict[str, Callable] = {
     "gemm_fwd": _case_gemm_fwd,
     "gemm_fwd_gelu": _case_gemm_fwd_gelu,
     "gemm_dgrad_dgelu": _case_gemm_dgrad_dgelu,
+    "gemm_resid_o": _resid_case(768, 768),
+    "gemm_resid_fc2": _resid_case(768, 3072),
     "gemm_wgrad": _case_gemm_wgrad,
     "gemm_8192": _case_gemm_8192,
     # every weight gradient of the 125M step (16384 tokens): fc1, fc2, out-proj, tied head

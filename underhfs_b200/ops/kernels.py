@@ -165,13 +165,27 @@ def matmul_bf16(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return c
 
 
+# fp32 products at least this large (M, N and K) run as 3xTF32 on the
+# tensor cores; smaller ones (and UHFS_F32_GEMM=simt) on the SIMT kernel
+_F32_TC_MIN = 256
+_F32_GEMM = os.environ.get("UHFS_F32_GEMM", "auto")
+
+
 def matmul_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """Exact fp32 c = a @ b (SIMT FMA kernel)."""
+    """fp32 c = a @ b.  Large products: three tf32 tensor-core products per
+    term (hi*hi + hi*lo + lo*hi of a tf32 split, fp32 accumulation), within a
+    few fp32 ulps of the exact dot product; small ones: exact SIMT FMA."""
     a = a.contiguous()
     b = b.contiguous()
     M, K = a.shape
     N = b.shape[1]
     c = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    if _F32_GEMM != "simt" and min(M, N, K) >= _F32_TC_MIN and N % 4 == 0:
+        kp = (K + 31) // 32 * 32
+        ws_a = torch.empty((M, 3 * kp), dtype=torch.float32, device=a.device)
+        ws_b = torch.empty((N, 3 * kp), dtype=torch.float32, device=a.device)
+        core().gemm_f32_3xtf32(ptr(a), ptr(b), ptr(c), M, N, K, False, ptr(ws_a), ptr(ws_b), stream())
+        return c
     core().gemm_f32(ptr(a), ptr(b), ptr(c), M, N, K, False, stream())
     return c
 
