@@ -404,6 +404,15 @@ __device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
   return d;
 }
 
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "mul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 __device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
   float2 d;
   asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
@@ -663,6 +672,34 @@ __device__ __forceinline__ float gelu_tanh_grad_fast(float x) {
   const float t = tanh_approx(u);
   const float du = k0 * fmaf(3.0f * k1, x2, 1.0f);
   return 0.5f * (1.0f + t) + 0.5f * x * fmaf(-t, t, 1.0f) * du;
+}
+
+// The same tanh-form GELU and its derivative on a pair of values with packed
+// f32x2 arithmetic (GEMM epilogues, where the per-element math bounds the
+// epilogue's issue rate):
+//   gelu(x)  = hx (1 + t),                  hx = x / 2
+//   gelu'(x) = (1 + t) / 2 * (1 + x du (1 - t)),
+//   t = tanh(x (k0 + k0 k1 x^2)),  du = k0 (1 + 3 k1 x^2)
+// (1 - t^2 = (1 - t)(1 + t) folds the two terms of the derivative).
+__device__ __forceinline__ float2 gelu_tanh_fast_x2(float2 x) {
+  const float k0 = 0.7978845608028654f, k0k1 = 0.7978845608028654f * 0.044715f;
+  const float2 x2 = f2_mul(x, x);
+  const float2 u = f2_mul(x, f2_fma(x2, make_float2(k0k1, k0k1), make_float2(k0, k0)));
+  const float2 t = make_float2(tanh_approx(u.x), tanh_approx(u.y));
+  const float2 hx = f2_mul(x, make_float2(0.5f, 0.5f));
+  return f2_fma(hx, t, hx);
+}
+
+__device__ __forceinline__ float2 gelu_tanh_grad_fast_x2(float2 x) {
+  const float k0 = 0.7978845608028654f, k0k1 = 0.7978845608028654f * 0.044715f;
+  const float2 x2 = f2_mul(x, x);
+  const float2 u = f2_mul(x, f2_fma(x2, make_float2(k0k1, k0k1), make_float2(k0, k0)));
+  const float2 t = make_float2(tanh_approx(u.x), tanh_approx(u.y));
+  const float2 du = f2_fma(x2, make_float2(3.0f * k0k1, 3.0f * k0k1), make_float2(k0, k0));
+  const float2 a = f2_mul(x, du);
+  const float2 c = f2_fma(a, f2_sub(make_float2(1.0f, 1.0f), t), make_float2(1.0f, 1.0f));
+  const float2 h = f2_fma(t, make_float2(0.5f, 0.5f), make_float2(0.5f, 0.5f));
+  return f2_mul(h, c);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

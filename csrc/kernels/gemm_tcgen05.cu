@@ -340,7 +340,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
       float u[32];
       unpack_bf16x32(aux.r[j], u);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= gelu_tanh_grad_fast(u[i]);
+      for (int i = 0; i < 32; i += 2) {
+        const float2 g = f2_mul(make_float2(v[i], v[i + 1]), gelu_tanh_grad_fast_x2(make_float2(u[i], u[i + 1])));
+        v[i] = g.x;
+        v[i + 1] = g.y;
+      }
     }
     if constexpr (kBoxes > 0) {
       uint8_t* box = box_base + (kBufs == 2 ? (int)(seq & 1u) * kBoxes * kEpiBox : 0);
@@ -363,7 +367,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
               make_uint4(pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]), pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]),
                          pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]), pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_fast(v[i]);
+        for (int i = 0; i < 32; i += 2) {
+          const float2 g = gelu_tanh_fast_x2(make_float2(v[i], v[i + 1]));
+          v[i] = g.x;
+          v[i + 1] = g.y;
+        }
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q)
@@ -1296,10 +1304,20 @@ bool pair_enabled() {
 // K >= 2048 (64 vs 70 us); with a short main loop the row-wise aux loads of
 // the residual / dGELU epilogues bound the tile and the single-CTA kernel is
 // 4-7 % faster.
+// Residual / dGELU epilogues go to CTA pairs from this K on
+// (UHFS_GEMM_PAIR_EPI_K overrides).
+int pair_epi_min_k() {
+  static const int k = [] {
+    const char* e = getenv("UHFS_GEMM_PAIR_EPI_K");
+    return e != nullptr ? atoi(e) : 2048;
+  }();
+  return k;
+}
+
 bool pair_preferred(const GemmProblem& p) {
   if (!pair_enabled()) return false;
   return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.epi == GEMM_EPI_F32_ACCUM ||
-         p.epi == GEMM_EPI_BIAS_GELU || p.K >= 2048;
+         p.epi == GEMM_EPI_BIAS_GELU || p.K >= pair_epi_min_k();
 }
 }  // namespace
 
