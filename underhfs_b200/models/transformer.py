@@ -26,6 +26,7 @@ blocks run backward.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Callable
 
@@ -161,6 +162,10 @@ def initial_value(spec: LMSpec, name: str, shape: tuple[int, ...], init: str, ge
 
 
 _SIDE_STREAMS: dict = {}
+
+
+# UNDERHFS_WGRAD_SIDE=0 keeps the weight-gradient GEMMs on the compute stream
+_WGRAD_SIDE = os.environ.get("UNDERHFS_WGRAD_SIDE", "1") != "0"
 
 
 def _side_stream(device) -> torch.cuda.Stream:
@@ -332,41 +337,52 @@ class LMEngine:
             dl = sv["logits"]
             # (p - onehot) / M * dL/dloss, computed in place over the kept logits
             K.softmax_cross_entropy(dl, sv["targets"], dl, 1.0 / M, loss_grad)
-        # head + final norm
-        self.unit_backward_begin("tail")
-        dhf = K.linear_dgrad(dl, self.Wh)
-        K.linear_wgrad_accum(dl, sv["hf"], self.gWh)
-        dx = K.rmsnorm_backward(dhf, sv["xL"], self.lnf, sv["rf"], None, self.g_lnf)
-        self.unit_backward_end("tail")
-        if hook is not None and not s.tied:
-            hook(*self.tail_range)
-        elif hook is not None:
-            hook(self.flat.by_name["norm.weight"].offset, self.flat.numel)
-        del dl, dhf
-        # Bias gradients are column sums of the output gradients: HBM-bound
-        # reductions launched on a side stream as soon as their input exists,
-        # so they run beside the compute-bound GEMMs of the same block; the
-        # compute stream joins the side stream at the end of the block (before
-        # the block's gradients are handed to the reduction hooks).
+        # Side stream: bias-gradient column sums (HBM-bound reductions) and,
+        # with _WGRAD_SIDE, the weight-gradient GEMMs, launched as soon as
+        # their inputs exist.  Nothing on the compute stream's critical path
+        # (dgrad -> attention -> dgrad) reads their outputs, so they fill the
+        # SMs the critical-path kernels leave idle (fill, tail, latency-bound
+        # phases); the compute stream joins the side stream at the end of each
+        # unit, before the unit's gradients are handed to the reduction hooks.
         flat = getattr(self, "flat", None)
         side = _side_stream(flat.device if flat is not None else None)
         pending: list = []
 
-        def colsum_async(x, out):
-            if out is None:
-                return
+        def on_side(fn, *keep):
             ready = torch.cuda.Event()
             ready.record()
             side.wait_event(ready)
             with torch.cuda.stream(side):
-                K.colsum_accum(x, out)
-            pending.append(x)  # kept alive until the join
+                fn()
+            pending.extend(keep)  # inputs kept alive until the join
+
+        def wgrad(dy, x, dw):
+            if _WGRAD_SIDE:
+                on_side(lambda: K.linear_wgrad_accum(dy, x, dw), dy, x)
+            else:
+                K.linear_wgrad_accum(dy, x, dw)
+
+        def colsum_async(x, out):
+            if out is not None:
+                on_side(lambda: K.colsum_accum(x, out), x)
 
         def join():
             if pending:
                 torch.cuda.current_stream().wait_stream(side)
                 pending.clear()
 
+        # head + final norm
+        self.unit_backward_begin("tail")
+        dhf = K.linear_dgrad(dl, self.Wh)
+        wgrad(dl, sv["hf"], self.gWh)
+        dx = K.rmsnorm_backward(dhf, sv["xL"], self.lnf, sv["rf"], None, self.g_lnf)
+        join()
+        self.unit_backward_end("tail")
+        if hook is not None and not s.tied:
+            hook(*self.tail_range)
+        elif hook is not None:
+            hook(self.flat.by_name["norm.weight"].offset, self.flat.numel)
+        del dl, dhf
         for bi in range(len(self.blocks) - 1, -1, -1):
             blk, saved = self.blocks[bi], sv["blocks"][bi]
             nvtx.push(f"bwd/block{bi}")
@@ -375,17 +391,17 @@ class LMEngine:
             # MLP
             colsum_async(dx, blk["gb2"])
             du = K.linear_dgrad(dx, blk["W2"], gelu_in=u)
-            K.linear_wgrad_accum(dx, g, blk["gW2"])
+            wgrad(dx, g, blk["gW2"])
             colsum_async(du, blk["gb1"])
             dh2 = K.linear_dgrad(du, blk["W1"])
-            K.linear_wgrad_accum(du, h2, blk["gW1"])
+            wgrad(du, h2, blk["gW1"])
             del du
             dx1 = K.rmsnorm_backward(dh2, x1, blk["ln2"], r2, dx, blk["g_ln2"])
             del dh2
             # attention
             colsum_async(dx1, blk["gbo"])
             do = K.linear_dgrad(dx1, blk["Wo"])
-            K.linear_wgrad_accum(dx1, o, blk["gWo"])
+            wgrad(dx1, o, blk["gWo"])
             if self.context_attention is not None:
                 dqkv = self.context_attention.backward(qkv, o, lse, do, B, T, H, D)
             else:
@@ -393,7 +409,7 @@ class LMEngine:
             del do
             colsum_async(dqkv, blk["gbqkv"])
             dh1 = K.linear_dgrad(dqkv, blk["Wqkv"])
-            K.linear_wgrad_accum(dqkv, h1, blk["gWqkv"])
+            wgrad(dqkv, h1, blk["gWqkv"])
             del dqkv
             dx = K.rmsnorm_backward(dh1, x, blk["ln1"], r1, dx1, blk["g_ln1"])
             del dh1, dx1
