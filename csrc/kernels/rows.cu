@@ -451,6 +451,10 @@ __global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* 
     }
   }
   mx = block_reduce_max(mx, sm);
+  // exp(x - mx) = 2^(x log2e - mx log2e): one FMA and one MUFU ex2 per
+  // logit, computed once; the exponentials replace the logits in `raw`
+  // (rounded to T, the gradient's own type) for the gradient pass
+  const float l2e = 1.4426950408889634f, mxl = mx * l2e;
   float sum = 0.f;
 #pragma unroll
   for (int k = 0; k < kCeVecs; ++k) {
@@ -458,7 +462,11 @@ __global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* 
       float f[8];
       unpack8<T>(raw[k], f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum += __expf(f[i] - mx);
+      for (int i = 0; i < 8; ++i) {
+        f[i] = ex2_approx(fmaf(f[i], l2e, -mxl));
+        sum += f[i];
+      }
+      raw[k] = pack8<T>(f);
     }
   }
   const long long tgt = targets[row];
@@ -485,7 +493,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) softmax_ce_reg_kernel(const T* 
       unpack8<T>(raw[k], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        f[i] = __expf(f[i] - mx) * inv;
+        f[i] *= inv;
         if ((long long)v * 8 + i == tgt) f[i] -= grad_scale;
       }
       __stcs(reinterpret_cast<uint4*>(dr) + v, pack8<T>(f));
