@@ -53,6 +53,26 @@ def _resid_case(n_out: int, n_in: int):
     return case
 
 
+def _resid_variant(block_n: int, cta_pair: int):
+    """The out-projection (768 x 768, K 768) residual GEMM with a forced tile
+    shape: block_n 128 or 256 on one SM, or the CTA pair."""
+    def case():
+        x, w, b, r = _bf(TOKENS, 768), _bf(768, 768, scale=0.03), _bf(768), _bf(TOKENS, 768)
+        out = torch.empty(TOKENS, 768, dtype=torch.bfloat16, device="cuda")
+        return (lambda: K.gemm_raw(TOKENS, 768, 768, x, 768, False, w, 768, False, out, 768, K.EPI_RESID, bias=b,
+                                   aux=r, ld_aux=768, block_n=block_n, cta_pair=cta_pair),
+                2.0 * TOKENS * 768 * 768, 0)
+    return case
+
+
+def _wgrad_split_case(n_out: int, n_in: int, splits: int):
+    def case():
+        dy, x = _bf(TOKENS, n_out), _bf(TOKENS, n_in)
+        dw = torch.zeros(n_out, n_in, device="cuda")
+        return lambda: K.linear_wgrad_accum(dy, x, dw, splits=splits), 2.0 * TOKENS * n_out * n_in, 0
+    return case
+
+
 def _case_gemm_dgrad_dgelu():
     dy, w, u = _bf(TOKENS, 768), _bf(768, 3072, scale=0.03), _bf(TOKENS, 3072)
     return lambda: K.linear_dgrad(dy, w, gelu_in=u), 2.0 * TOKENS * 3072 * 768, 0
@@ -206,6 +226,11 @@ CASES: dict[str, Callable] = {
     "gemm_dgrad_dgelu": _case_gemm_dgrad_dgelu,
     "gemm_resid_o": _resid_case(768, 768),
     "gemm_resid_fc2": _resid_case(768, 3072),
+    "gemm_resid_o_bn128": _resid_variant(128, 0),
+    "gemm_resid_o_pair": _resid_variant(256, 1),
+    "wgrad_o_split8": _wgrad_split_case(768, 768, 8),
+    "wgrad_o_split16": _wgrad_split_case(768, 768, 16),
+    "wgrad_qkv_split4": _wgrad_split_case(2304, 768, 4),
     "gemm_wgrad": _case_gemm_wgrad,
     "gemm_8192": _case_gemm_8192,
     # every weight gradient of the 125M step (16384 tokens): fc1, fc2, out-proj, tied head
