@@ -65,6 +65,17 @@ def _resid_variant(block_n: int, cta_pair: int):
     return case
 
 
+def _plain_case(n_out: int, n_in: int, pair: int):
+    """Linear without bias or epilogue operand, for comparison with the
+    residual variant of the same shape."""
+    def case():
+        x, w = _bf(TOKENS, n_in), _bf(n_out, n_in, scale=0.03)
+        out = torch.empty(TOKENS, n_out, dtype=torch.bfloat16, device="cuda")
+        return (lambda: K.gemm_raw(TOKENS, n_out, n_in, x, n_in, False, w, n_in, False, out, n_out, K.EPI_BF16,
+                                   cta_pair=pair), 2.0 * TOKENS * n_out * n_in, 0)
+    return case
+
+
 def _wgrad_split_case(n_out: int, n_in: int, splits: int):
     def case():
         dy, x = _bf(TOKENS, n_out), _bf(TOKENS, n_in)
@@ -228,6 +239,8 @@ CASES: dict[str, Callable] = {
     "gemm_resid_fc2": _resid_case(768, 3072),
     "gemm_resid_o_bn128": _resid_variant(128, 0),
     "gemm_resid_o_pair": _resid_variant(256, 1),
+    "gemm_o_plain": _plain_case(768, 768, -1),
+    "gemm_o_plain_single": _plain_case(768, 768, 0),
     "wgrad_o_split8": _wgrad_split_case(768, 768, 8),
     "wgrad_o_split16": _wgrad_split_case(768, 768, 16),
     "wgrad_qkv_split4": _wgrad_split_case(2304, 768, 4),
