@@ -98,6 +98,19 @@ class StepMeter:
                 "max_memory_gb": torch.cuda.max_memory_allocated() / 2**30}
 
 
+class PendingLoss:
+    """A step's loss on its way to the host: the device-to-host copy is queued
+    on the stream behind the step, and result() waits for that copy only."""
+
+    def __init__(self, host: torch.Tensor, ready: torch.cuda.Event) -> None:
+        self._host = host
+        self._ready = ready
+
+    def result(self) -> float:
+        self._ready.synchronize()
+        return float(self._host.item())
+
+
 class Trainer:
     def __init__(self, model, cfg: TrainConfig, *, policy=None) -> None:
         from underhfs_b200.distributed import DistributedDataParallel, policy_from_env
@@ -224,9 +237,15 @@ class Trainer:
 
         return (shard_sequence(ids, self.cp.rank, self.cp.size), shard_sequence(targets, self.cp.rank, self.cp.size))
 
-    def step_from_host(self, host_batch: torch.Tensor) -> float:
+    def step_from_host(self, host_batch: torch.Tensor, *, wait: bool = True):
         """End-to-end step: pinned host [2, B, T] int64 batch in, host float loss out.
-        With context parallelism every rank passes the same full sequences."""
+        With context parallelism every rank passes the same full sequences.
+
+        ``wait=False`` queues the step and the copy of its loss to pinned host
+        memory and returns a PendingLoss at once, so the host can queue the
+        next step before reading this one's loss (``.result()``).  A
+        PendingLoss stays valid until two more asynchronous steps have been
+        queued; the host batch must not change until its result() returned."""
         if self.cp is not None:
             self._full_batch.copy_(host_batch, non_blocking=True)
             ids, tg = self.local_batch(self._full_batch[0], self._full_batch[1])
@@ -235,7 +254,17 @@ class Trainer:
         else:
             self.static_batch.copy_(host_batch, non_blocking=True)
         loss = self.step(self.static_batch[0], self.static_batch[1])
-        return float(loss.item())
+        if wait:
+            return float(loss.item())
+        if not hasattr(self, "_loss_ring"):
+            self._loss_ring = [torch.empty((), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+            self._ring_pos = 0
+        host = self._loss_ring[self._ring_pos]
+        self._ring_pos ^= 1
+        host.copy_(loss.detach().reshape(()).float(), non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record()
+        return PendingLoss(host, ready)
 
     def release(self) -> None:
         """Drop the captured graph and, at ZeRO stage 3, the sharded runtime's
