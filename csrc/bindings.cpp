@@ -423,6 +423,7 @@ PYBIND11_MODULE(_core, m) {
 
   m.def("set_attn_bwd_trace", [](uintptr_t buf) { set_attn_bwd_trace(P<unsigned long long>(buf)); });
   m.def("set_attn_fwd_trace", [](uintptr_t buf) { set_attn_fwd_trace(P<unsigned long long>(buf)); });
+  m.def("set_gemm_trace", [](uintptr_t buf) { set_gemm_trace(P<unsigned long long>(buf)); });
 
   m.def("raster_iso", [](uintptr_t quads, uintptr_t colors, int n, uintptr_t order, uintptr_t rgba, int w, int h,
                          uintptr_t s) {

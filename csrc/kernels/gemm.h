@@ -71,6 +71,10 @@ struct GemmProblem {
 
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream);
 
+// Trace builds (-DUHFS_GEMM_TRACE): per-unit clock stamps of CTA 0 of the
+// single-CTA kernel into buf[event * 16 + unit] (8 events); nullptr turns it off.
+void set_gemm_trace(unsigned long long* buf);
+
 // fp32 C[M,N] (row stride ldc) = A[M,K] B[N,K]^T with tf32 tensor-core math
 // (both operands K-major fp32, rows 16-byte aligned, strides multiples of 4).
 void gemm_tf32_tcgen05(const float* A, long long lda, const float* B, long long ldb, float* C, long long ldc, int M,

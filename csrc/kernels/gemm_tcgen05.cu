@@ -82,7 +82,29 @@ struct GemmArgs {
   long long ld_aux_out;
   DeviceStatus* status;
   GemmGather ag;
+  unsigned long long* trace;  // UHFS_GEMM_TRACE builds: clock stamps of CTA 0 (set_gemm_trace)
 };
+
+// Per-unit clock64 stamps of CTA 0 of the single-CTA kernel, compiled in only
+// with -DUHFS_GEMM_TRACE (UNDERHFS_GEMM_TRACE=1 at build time):
+// trace[event * kGemmTraceUnits + unit].
+constexpr int kGemmTraceUnits = 16;
+enum GemmTraceEvent {
+  kGtProdStart = 0, kGtProdLast, kGtMmaAccFree, kGtMmaFirstFull, kGtMmaCommit, kGtEpiFull, kGtEpiRelease, kGtEpiDone,
+  kGtEvents
+};
+unsigned long long* g_gemm_trace = nullptr;
+#ifdef UHFS_GEMM_TRACE
+#define GEMM_TRACE(ev, u)                                                                                 \
+  do {                                                                                                    \
+    if (args.trace != nullptr && blockIdx.x == 0 && (u) < kGemmTraceUnits)                                \
+      args.trace[(ev) * kGemmTraceUnits + (u)] = (unsigned long long)clock64();                           \
+  } while (0)
+#else
+#define GEMM_TRACE(ev, u) \
+  do {                    \
+  } while (0)
+#endif
 
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
   uint32_t v;
@@ -466,8 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
       int tm, tn, kb0, kb1;
+      int pu = 0;  // units started (trace index)
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         const int m0 = tm * BM, n0 = tn * BN;
+        GEMM_TRACE(kGtProdStart, pu);
         if (!UHFS_CHECK(m0 < args.M && n0 < args.N && kb0 < kb1 && kb1 <= args.kb_total, args.status, 12)) {
           ok = false;
           break;
@@ -509,6 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        GEMM_TRACE(kGtProdLast, pu);
+        ++pu;
       }
       // Never leave the CTA with bulk copies still landing in shared memory.
       for (int s = 0; s < S; ++s)
@@ -524,8 +550,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
       int tm, tn, kb0, kb1;
+      [[maybe_unused]] int mu = 0;  // units issued (trace index)
       while (ok && unit_next(args, it, tm, tn, kb0, kb1)) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, args.status, kErrWaitTimeoutAccum, 20)) break;
+        GEMM_TRACE(kGtMmaAccFree, mu);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -533,6 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (kb == kb0) GEMM_TRACE(kGtMmaFirstFull, mu);
           tc_fence_after();
           const uint32_t a_base = smem_u32(tiles + stage * Cfg::kStageBytes);
           const uint32_t b_base = a_base + Cfg::kABytes;
@@ -557,6 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        GEMM_TRACE(kGtMmaCommit, mu);
+        ++mu;
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -630,17 +661,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t seq = 0;
     UnitIter it = unit_begin(args, (int)blockIdx.x, (int)gridDim.x);
     int tm, tn, kb0, kb1;
+    [[maybe_unused]] const bool tracer = warp == 2 && lane == 0;
+    [[maybe_unused]] int eu = 0;  // units finished (trace index)
     while (unit_next(args, it, tm, tn, kb0, kb1)) {
       const int m0 = tm * BM, n0 = tn * BN;
       AuxRegs<BN> aux;
       epi_load_aux<BN, EPI>(args, m0, n0, quarter, ehalf, lane, 0, aux.r[0]);
       if (!mbar_wait_warp(&tfull[acc], acc_phase, args.status, kErrWaitTimeoutAccum, 30)) break;
+      if (tracer) GEMM_TRACE(kGtEpiFull, eu);
       tc_fence_after();
       epilogue_tile<BN, EPI, 1>(args, &tmC, &tmAuxOut, tmem_base + (uint32_t)(acc * BN), m0, n0, quarter, ehalf,
                                 lane, box, seq, aux, [&] {
                                   tc_fence_before();
                                   mbar_arrive(&tempty[acc]);
+                                  if (tracer) GEMM_TRACE(kGtEpiRelease, eu);
                                 });
+      if (tracer) GEMM_TRACE(kGtEpiDone, eu);
+      ++eu;
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -1084,6 +1121,7 @@ void launch(const GemmProblem& p, cudaStream_t stream) {
   a.stream_k = (EPI == GEMM_EPI_F32_ACCUM && p.splits == 0) ? 1 : 0;
   a.sk_chunk = a.stream_k ? stream_k_chunk() : 0;
   a.group = raster_group();
+  a.trace = g_gemm_trace;
   int splits = p.splits < 1 ? 1 : p.splits;
   if (splits > a.kb_total) splits = a.kb_total;
   a.kb_per_split = (a.kb_total + splits - 1) / splits;
@@ -1351,6 +1389,16 @@ CUtensorMap make_tmap_f32_2d(const void* base, uint64_t inner, uint64_t outer, u
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return m;
+}
+
+void set_gemm_trace(unsigned long long* buf) {
+#ifdef UHFS_GEMM_TRACE
+  g_gemm_trace = buf;
+#else
+  if (buf != nullptr)
+    throw std::runtime_error("set_gemm_trace: the extension was built without UHFS_GEMM_TRACE "
+                             "(rebuild with UNDERHFS_GEMM_TRACE=1)");
+#endif
 }
 
 void gemm_tf32_tcgen05(const float* A, long long lda, const float* B, long long ldb, float* C, long long ldc, int M,

@@ -68,6 +68,10 @@ def _check_flags() -> str:
     # (kernel_cases attn_fwd / attn_bwd --trace); never in the product build
     if os.environ.get("UNDERHFS_ATTN_TRACE", "0") == "1":
         flags += "-DUHFS_ATTN_TRACE "
+    # UNDERHFS_GEMM_TRACE=1: per-unit clock64 stamps in the single-CTA GEMM
+    # (kernel_cases <gemm case> --trace); never in the product build
+    if os.environ.get("UNDERHFS_GEMM_TRACE", "0") == "1":
+        flags += "-DUHFS_GEMM_TRACE "
     return flags + _option_flags()
 
 

@@ -355,17 +355,58 @@ def trace_attn_fwd(ctas=(0, 2)) -> str:
     return "\n".join(out)
 
 
+GEMM_TRACE_EVENTS = ("prodStart", "prodLast", "mmaAccFree", "mmaFirstFull", "mmaCommit", "epiFull", "epiRelease",
+                     "epiDone")
+
+
+def trace_gemm(name: str) -> str:
+    """Run one GEMM case with the single-CTA kernel's per-unit clock stamps
+    (CTA 0; build with UNDERHFS_GEMM_TRACE=1): SM cycles from the first stamp
+    for each unit the CTA processed."""
+    fn, _, _ = CASES[name]()
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    buf = torch.zeros(len(GEMM_TRACE_EVENTS) * 16, dtype=torch.int64, device="cuda")
+    K.core().set_gemm_trace(buf.data_ptr())
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        K.core().set_gemm_trace(0)
+    tr = buf.view(len(GEMM_TRACE_EVENTS), 16).cpu()
+    nz = tr[tr != 0]
+    if nz.numel() == 0:
+        return f"{name}: no stamps (single-CTA kernel not used, or a build without UHFS_GEMM_TRACE)"
+    t0 = int(nz.min())
+    out = [f"{name}: CTA 0, SM cycles from its first stamp",
+           "  unit " + " ".join(f"{e:>12s}" for e in GEMM_TRACE_EVENTS)]
+    for u in range(16):
+        if int(tr[:, u].abs().sum()) == 0:
+            continue
+        out.append(f"  {u:4d} " + " ".join(f"{int(tr[e, u]) - t0:12d}" if int(tr[e, u]) else f"{'-':>12s}"
+                                           for e in range(len(GEMM_TRACE_EVENTS))))
+    return "\n".join(out)
+
+
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", nargs="+", choices=sorted(CASES) + ["all"], help="one or more cases, or all")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", action="store_true", help="print CUDA-event time per launch")
-    ap.add_argument("--trace", action="store_true", help="attn_bwd: print the kernel's per-step clock stamps")
+    ap.add_argument("--trace", action="store_true",
+                    help="attn_fwd / attn_bwd / gemm_*: print the kernel's clock stamps (trace builds)")
     args = ap.parse_args(argv)
     torch.manual_seed(0)
     if args.trace:
+        if any(c.startswith("gemm_") for c in args.case):
+            for c in args.case:
+                print(trace_gemm(c))
+            st = K.core().device_status(True)
+            print("ok" if st["code"] == 0 else f"device status {st}")
+            return 0 if st["code"] == 0 else 1
         if len(args.case) != 1 or args.case[0] not in ("attn_bwd", "attn_fwd"):
-            ap.error("--trace is available for attn_fwd and attn_bwd")
+            ap.error("--trace is available for attn_fwd, attn_bwd and the gemm_* cases")
         print(trace_attn_bwd() if args.case[0] == "attn_bwd" else trace_attn_fwd())
         st = K.core().device_status(True)
         print("ok" if st["code"] == 0 else f"device status {st}")
