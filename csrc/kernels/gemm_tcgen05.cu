@@ -266,12 +266,14 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
   }
 }
 
-// Epilogue operands that are read row-wise (the residual of GEMM_EPI_RESID,
+// Epilogue operands read per output element (the residual of GEMM_EPI_RESID,
 // the GELU input of GEMM_EPI_DGELU): each lane needs 64 bytes of its row per
-// 32-column chunk.  Chunk 0 is loaded before the warp waits for the
-// accumulator and chunk j + 1 while chunk j is processed.  (Requesting every
-// chunk up front was measured slower: 116.5 against 91.9 us for the
-// 16384 x 3072 x 768 dGELU product.)
+// 32-column chunk.  They are loaded coalesced (eight rows per instruction;
+// one row per lane cost 32 L1 wavefronts per instruction and made these
+// epilogues longer than their tiles' main loops, per the per-unit clock
+// trace) and regrouped by row through the warp's store box.  Chunk 0 is
+// loaded before the warp waits for the accumulator and chunk j + 1 while
+// chunk j is processed.
 template <int BN>
 struct AuxRegs {
   uint4 r[BN / 64][4];
@@ -286,20 +288,41 @@ __device__ __forceinline__ int epi_c_end(const GemmArgs& args, int BN, int n0, i
   return min((ehalf + 1) * (BN / 64), (args.N - n0 + 31) / 32);
 }
 
-// Load chunk j of this warp's columns (zeros outside the matrix).
+// Load chunk j of this warp's columns (zeros outside the matrix), coalesced:
+// piece q of lane l is row 8q + l/4 of the warp's 32 rows, 16-byte column
+// group l % 4, so one load instruction covers eight whole 64-byte row
+// segments.  epi_aux_to_rows() regroups the pieces by row through the
+// warp's store box.
 template <int BN, int EPI>
 __device__ __forceinline__ void epi_load_aux(const GemmArgs& args, int m0, int n0, int quarter, int ehalf, int lane,
                                              int j, uint4* r) {
   if constexpr (epi_reads_aux<EPI>()) {
-    const int row = m0 + quarter * 32 + lane;
     const int c = ehalf * (BN / 64) + j;
-    const int col0 = n0 + c * 32;
-    const bool ok = row < args.M && c < epi_c_end(args, BN, n0, ehalf);
-    const __nv_bfloat16* src = args.aux + (long long)row * args.ld_aux + col0;
+    const int col = n0 + c * 32 + (lane & 3) * 8;
+    const bool ok = c < epi_c_end(args, BN, n0, ehalf) && col < args.N;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      r[q] = (ok && col0 + q * 8 < args.N) ? *reinterpret_cast<const uint4*>(src + q * 8) : make_uint4(0u, 0u, 0u, 0u);
+    for (int q = 0; q < 4; ++q) {
+      const int row = m0 + quarter * 32 + q * 8 + (lane >> 2);
+      r[q] = (ok && row < args.M) ? *reinterpret_cast<const uint4*>(args.aux + (long long)row * args.ld_aux + col)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+    }
   }
+}
+
+// The coalesced pieces of epi_load_aux -> this lane's own row (64 bytes as
+// four 16-byte groups), through the warp's 32 x 64-byte box in the layout
+// of the output rows (16-byte group g of row r at (g ^ ((r >> 1) & 3)) << 4).
+// The box must be free (its last TMA store has read it).
+__device__ __forceinline__ void epi_aux_to_rows(uint8_t* box, int lane, uint4* r) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int rr = q * 8 + (lane >> 2), g = lane & 3;
+    *reinterpret_cast<uint4*>(box + rr * 64 + ((g ^ ((rr >> 1) & 3)) << 4)) = r[q];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) r[q] = *reinterpret_cast<const uint4*>(box + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+  __syncwarp();
 }
 
 __device__ __forceinline__ void unpack_bf16x32(const uint4* raw, float* v) {
@@ -352,6 +375,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += b[i];
       }
+    }
+    if constexpr (epi_reads_aux<EPI>()) {
+      // the box this chunk will store from must be free before it regroups
+      // the operand rows (the store wait below then returns at once)
+      uint8_t* tb = box_base + (kBufs == 2 ? (int)(seq & 1u) * kBoxes * kEpiBox : 0);
+      if (lane == 0) {
+        if constexpr (kBufs == 2)
+          bulk_wait_group_read1();
+        else
+          bulk_wait_group_read0();
+      }
+      __syncwarp();
+      epi_aux_to_rows(tb, lane, aux.r[j]);
     }
     if constexpr (EPI == GEMM_EPI_RESID) {
       float r[32];
