@@ -72,7 +72,7 @@ struct GemmProblem {
 void gemm_bf16_tcgen05(const GemmProblem& p, cudaStream_t stream);
 
 // Trace builds (-DUHFS_GEMM_TRACE): per-unit clock stamps of CTA 0 of the
-// single-CTA kernel into buf[event * 16 + unit] (8 events); nullptr turns it off.
+// single-CTA kernel into buf[event * 16 + unit] (20 events); nullptr turns it off.
 void set_gemm_trace(unsigned long long* buf);
 
 // fp32 C[M,N] (row stride ldc) = A[M,K] B[N,K]^T with tf32 tensor-core math

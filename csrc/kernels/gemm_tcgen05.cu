@@ -91,7 +91,10 @@ struct GemmArgs {
 constexpr int kGemmTraceUnits = 16;
 enum GemmTraceEvent {
   kGtProdStart = 0, kGtProdLast, kGtMmaAccFree, kGtMmaFirstFull, kGtMmaCommit, kGtEpiFull, kGtEpiRelease, kGtEpiDone,
-  kGtEvents
+  kGtChunkLd,                        // + j: chunk j's accumulator columns in registers
+  kGtChunkMath = kGtChunkLd + 4,     // + j: chunk j's values final (bias, operand, activation)
+  kGtChunkStore = kGtChunkMath + 4,  // + j: chunk j's TMA store issued
+  kGtEvents = kGtChunkStore + 4
 };
 unsigned long long* g_gemm_trace = nullptr;
 #ifdef UHFS_GEMM_TRACE
@@ -349,7 +352,8 @@ template <int BN, int EPI, int kBufs, class Release>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtensorMap* tmC, const CUtensorMap* tmAuxOut,
                                               uint32_t tmem_acc, int m0, int n0, int quarter, int ehalf, int lane,
                                               uint8_t* box_base, uint32_t& seq, AuxRegs<BN>& aux,
-                                              Release release) {
+                                              Release release, [[maybe_unused]] bool tracer = false,
+                                              [[maybe_unused]] int unit = 0) {
   constexpr int kBoxes = epi_boxes(EPI);
   const int row = m0 + quarter * 32 + lane;
   const bool row_ok = row < args.M;
@@ -364,6 +368,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
     const uint32_t taddr = tmem_acc + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32);
     tmem_ld_32x32b_x32(taddr, v);
     tc_wait_ld();
+    if (tracer && j < 4) GEMM_TRACE(kGtChunkLd + j, unit);
     if (c == c_end - 1) {
       release();  // the whole accumulator of this warp is in registers
     }
@@ -404,6 +409,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
         v[i + 1] = g.y;
       }
     }
+    if (tracer && j < 4) GEMM_TRACE(kGtChunkMath + j, unit);
     if constexpr (kBoxes > 0) {
       uint8_t* box = box_base + (kBufs == 2 ? (int)(seq & 1u) * kBoxes * kEpiBox : 0);
       ++seq;
@@ -444,6 +450,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const CUtens
         if constexpr (EPI == GEMM_EPI_BIAS_GELU) tma_store_2d(tmAuxOut, box + kEpiBox, col0, m0 + quarter * 32);
         bulk_commit_group();
       }
+      if (tracer && j < 4) GEMM_TRACE(kGtChunkStore + j, unit);
     } else if constexpr (EPI == GEMM_EPI_F32_ACCUM) {
       if (row_ok) {
         float* dst = reinterpret_cast<float*>(args.C) + (long long)row * args.ldc + col0;
@@ -711,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   tc_fence_before();
                                   mbar_arrive(&tempty[acc]);
                                   if (tracer) GEMM_TRACE(kGtEpiRelease, eu);
-                                });
+                                }, tracer, eu);
       if (tracer) GEMM_TRACE(kGtEpiDone, eu);
       ++eu;
       if (++acc == 2) {

@@ -356,7 +356,8 @@ def trace_attn_fwd(ctas=(0, 2)) -> str:
 
 
 GEMM_TRACE_EVENTS = ("prodStart", "prodLast", "mmaAccFree", "mmaFirstFull", "mmaCommit", "epiFull", "epiRelease",
-                     "epiDone")
+                     "epiDone", "ld0", "ld1", "ld2", "ld3", "math0", "math1", "math2", "math3", "st0", "st1", "st2",
+                     "st3")
 
 
 def trace_gemm(name: str) -> str:
@@ -380,11 +381,11 @@ def trace_gemm(name: str) -> str:
         return f"{name}: no stamps (single-CTA kernel not used, or a build without UHFS_GEMM_TRACE)"
     t0 = int(nz.min())
     out = [f"{name}: CTA 0, SM cycles from its first stamp",
-           "  unit " + " ".join(f"{e:>12s}" for e in GEMM_TRACE_EVENTS)]
+           "  unit " + " ".join(f"{e:>7s}" for e in GEMM_TRACE_EVENTS)]
     for u in range(16):
         if int(tr[:, u].abs().sum()) == 0:
             continue
-        out.append(f"  {u:4d} " + " ".join(f"{int(tr[e, u]) - t0:12d}" if int(tr[e, u]) else f"{'-':>12s}"
+        out.append(f"  {u:4d} " + " ".join(f"{int(tr[e, u]) - t0:7d}" if int(tr[e, u]) else f"{'-':>7s}"
                                            for e in range(len(GEMM_TRACE_EVENTS))))
     return "\n".join(out)
 
