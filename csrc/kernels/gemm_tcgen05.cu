@@ -1385,8 +1385,10 @@ bool pair_enabled() {
 // K >= 2048 (64 vs 70 us); with a short main loop the row-wise aux loads of
 // the residual / dGELU epilogues bound the tile and the single-CTA kernel is
 // 4-7 % faster.
-// Residual / dGELU epilogues go to CTA pairs from this K on
-// (UHFS_GEMM_PAIR_EPI_K overrides).
+// Residual epilogues go to CTA pairs from this K on (UHFS_GEMM_PAIR_EPI_K
+// overrides); with coalesced operand loads the dGELU epilogue is faster on
+// pairs at any K (fc2 dgrad, K = 768: 80.0 against 83.0 us) while the K = 768
+// residual GEMM is not (27.7 against 25.9 us).
 int pair_epi_min_k() {
   static const int k = [] {
     const char* e = getenv("UHFS_GEMM_PAIR_EPI_K");
@@ -1398,7 +1400,7 @@ int pair_epi_min_k() {
 bool pair_preferred(const GemmProblem& p) {
   if (!pair_enabled()) return false;
   return p.epi == GEMM_EPI_BF16 || p.epi == GEMM_EPI_F32_STORE || p.epi == GEMM_EPI_F32_ACCUM ||
-         p.epi == GEMM_EPI_BIAS_GELU || p.K >= pair_epi_min_k();
+         p.epi == GEMM_EPI_BIAS_GELU || p.epi == GEMM_EPI_DGELU || p.K >= pair_epi_min_k();
 }
 }  // namespace
 
