@@ -720,7 +720,7 @@ def run_reference_micro(args) -> int:
             out.append({"error": (proc.stderr.strip().splitlines() or ["?"])[-1]})
         return out
 
-    if rank == 0:
+    if world == 1:  # the single-GPU ops; with N > 1 ranks only the collectives run
         rows += run([iters, warm, 0], 900)
     if world > 1:
         import torch.distributed as dist
