@@ -671,6 +671,15 @@ if not with_coll:
         emit(op="run_microbenchmarks", **r.to_dict())
 else:
     rank, world, uid, max_bytes = int(sys.argv[4]), int(sys.argv[5]), sys.argv[6], int(sys.argv[7])
+    if rank == 0:
+        # NCCL's bootstrap root lives in the process that made the id: rank 0
+        # makes it here and hands it to the others through the file named in uid
+        import os
+        tmp = uid + ".tmp"
+        with open(tmp, "w") as f:
+            f.write(core.nccl_create_unique_id_hex())
+        os.replace(tmp, uid)
+        uid = open(uid).read().strip()
     pg = core.NcclProcessGroup(rank, world, uid)
     nbytes = 1024
     while nbytes <= max_bytes:
@@ -726,13 +735,33 @@ def run_reference_micro(args) -> int:
         import torch.distributed as dist
 
         dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
-        uid = [None]
-        if rank == 0:
-            uid[0] = subprocess.run([sys.executable, "-c", "from underhfs import _core; print(_core.nccl_create_unique_id_hex())"],
-                                    cwd=str(ref), env=env, capture_output=True, text=True).stdout.strip()
-        dist.broadcast_object_list(uid, src=0)
         max_bytes = int(os.environ.get("UNDERHFS_REF_COLL_MAX_BYTES", str(64 << 20)))
-        coll = run([iters, warm, 1, rank, world, uid[0], max_bytes], 1800)
+        argv = [iters, warm, 1, rank, world]
+        if rank == 0:
+            # rank 0's subprocess creates the NCCL id (its bootstrap root must
+            # stay alive) and writes it to a file; the id then goes to the
+            # other ranks through the process group
+            id_file = Path(tempfile.mkdtemp()) / "nccl_id"
+            proc = subprocess.Popen([sys.executable, "-c", _REF_MICRO, *map(str, argv + [id_file, max_bytes])],
+                                    cwd=str(ref), env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            deadline = time.time() + 120
+            while not id_file.exists() and proc.poll() is None and time.time() < deadline:
+                time.sleep(0.05)
+            uid = [id_file.read_text().strip() if id_file.exists() else ""]
+            dist.broadcast_object_list(uid, src=0)
+            try:
+                out, err = proc.communicate(timeout=1800)
+            except subprocess.TimeoutExpired:
+                proc.kill()
+                out, err = proc.communicate()
+            coll = [json.loads(l) for l in out.splitlines() if l.startswith("{")]
+            if proc.returncode != 0:
+                coll.append({"error": (err.strip().splitlines() or ["?"])[-1]})
+        else:
+            uid = [None]
+            dist.broadcast_object_list(uid, src=0)
+            coll = run(argv + [uid[0] or "missing", max_bytes], 1800) if uid[0] else [
+                {"error": "rank 0 could not create an NCCL id"}]
         gathered = [None] * world
         dist.all_gather_object(gathered, coll)
         dist.destroy_process_group()
