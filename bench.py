@@ -757,6 +757,9 @@ def run_reference_micro(args) -> int:
             coll = [json.loads(l) for l in out.splitlines() if l.startswith("{")]
             if proc.returncode != 0:
                 coll.append({"error": (err.strip().splitlines() or ["?"])[-1]})
+            import shutil
+
+            shutil.rmtree(id_file.parent, ignore_errors=True)
         else:
             uid = [None]
             dist.broadcast_object_list(uid, src=0)
